@@ -1,0 +1,547 @@
+// elementwise.cu -- broadcast binary ops, unary ops, their fused backward
+// rules, broadcast_to, fill and axpy for sm_100a.
+//
+// Every kernel here is HBM-bandwidth-bound (<= 1 flop per 4 bytes moved), so
+// the design is about bytes in flight and instruction count per byte:
+//  * flat paths (same shape, scalar operand): 128-bit loads/stores, four
+//    independent float4 per thread per iteration, grid = a multiple of the SM
+//    count with a grid-stride loop;
+//  * every other broadcast layout: dimensions are collapsed on the host, the
+//    innermost run of L elements is a "row", and each CTA resolves the operand
+//    offsets of a tile of rows ONCE into shared memory (what the reference's
+//    CPU kernel does per row, src/cpu/cpu_backend.cpp:59-105) and then streams
+//    the tile, 128-bit wide when the row layout allows. Offsets are 64-bit:
+//    config 5 has 2^32 outputs.
+// Arithmetic is the reference's (src/cpu/cpu_backend.cpp:24-27, 291-316),
+// compiled with -fmad=false and IEEE division so add/sub/mul/div/neg/relu
+// are bit-identical to the CPU path; exp/log/sigmoid use CUDA's
+// full-precision expf/logf.
+#include "vc_internal.cuh"
+
+#include <algorithm>
+#include <vector>
+
+namespace vc {
+
+// ---------------------------------------------------------------------------
+// Scalar arithmetic, exactly as the reference writes it.
+// ---------------------------------------------------------------------------
+template <int OP>
+__device__ __forceinline__ float bop(float x, float y) {
+    if constexpr (OP == VC_ADD) return x + y;
+    else if constexpr (OP == VC_SUB) return x - y;
+    else if constexpr (OP == VC_MUL) return x * y;
+    else return x / y;
+}
+
+template <int OP>
+__device__ __forceinline__ float uop(float x) {
+    if constexpr (OP == VC_NEG) return -x;
+    else if constexpr (OP == VC_RELU) return x > 0.0f ? x : 0.0f;
+    else if constexpr (OP == VC_RELU_GRAD) return x > 0.0f ? 1.0f : 0.0f;
+    else if constexpr (OP == VC_SIGMOID) {
+        // Branchy form of cpu_backend.cpp:302-307 (keeps exp from overflowing).
+        if (x >= 0.0f) return 1.0f / (1.0f + expf(-x));
+        const float e = expf(x);
+        return e / (1.0f + e);
+    } else if constexpr (OP == VC_EXP) return expf(x);
+    else return logf(x);
+}
+
+// Backward rules of src/ops.cpp (negate :158-164, exp :360-367, log
+// :369-376, relu :395-403, sigmoid :405-413), each one fused pass.
+template <int OP>
+__device__ __forceinline__ float ubwd(float x, float y, float g) {
+    if constexpr (OP == VC_NEG) return -g;
+    else if constexpr (OP == VC_EXP) return g * y;
+    else if constexpr (OP == VC_LOG) return g / x;
+    else if constexpr (OP == VC_RELU) return g * (x > 0.0f ? 1.0f : 0.0f);
+    else {  // VC_SIGMOID: gradient * y * (1.0F - y), left to right
+        const float gy = g * y;
+        const float one_minus = 1.0f - y;
+        return gy * one_minus;
+    }
+}
+
+template <int OP>
+__device__ __forceinline__ float4 bop4(float4 x, float4 y) {
+    return make_float4(bop<OP>(x.x, y.x), bop<OP>(x.y, y.y), bop<OP>(x.z, y.z), bop<OP>(x.w, y.w));
+}
+
+constexpr unsigned kThreads = 256;
+constexpr int kUnroll = 4;
+
+// ---------------------------------------------------------------------------
+// Flat binary: MODE 0 same shape, 1 scalar rhs, 2 scalar lhs. The scalar is
+// *sp when sp is not null (a one-element device tensor) else sv.
+// VEC: all pointers 16-byte aligned.
+// ---------------------------------------------------------------------------
+template <int OP, int MODE, bool VEC>
+__global__ void __launch_bounds__(kThreads)
+binary_flat_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                   float* __restrict__ out, std::size_t n, const float* __restrict__ sp, float sv) {
+    const float s = sp ? __ldg(sp) : sv;
+    const std::size_t tid = static_cast<std::size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const std::size_t stride = static_cast<std::size_t>(gridDim.x) * blockDim.x;
+    if constexpr (VEC) {
+        const std::size_t n4 = n >> 2;
+        const float4 s4 = make_float4(s, s, s, s);
+        std::size_t i = tid;
+        for (; i + (kUnroll - 1) * stride < n4; i += kUnroll * stride) {
+            float4 x[kUnroll], y[kUnroll];
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const std::size_t k = (i + u * stride) * 4;
+                x[u] = MODE == 2 ? s4 : ld4_stream(a + k);
+                y[u] = MODE == 1 ? s4 : ld4_stream(b + k);
+            }
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) st4_stream(out + (i + u * stride) * 4, bop4<OP>(x[u], y[u]));
+        }
+        for (; i < n4; i += stride) {
+            const std::size_t k = i * 4;
+            const float4 x = MODE == 2 ? s4 : ld4_stream(a + k);
+            const float4 y = MODE == 1 ? s4 : ld4_stream(b + k);
+            st4_stream(out + k, bop4<OP>(x, y));
+        }
+        for (std::size_t k = n4 * 4 + tid; k < n; k += stride)
+            out[k] = bop<OP>(MODE == 2 ? s : a[k], MODE == 1 ? s : b[k]);
+    } else {
+        for (std::size_t k = tid; k < n; k += stride)
+            out[k] = bop<OP>(MODE == 2 ? s : a[k], MODE == 1 ? s : b[k]);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Tiled strided broadcast. The collapsed output is [rows, L]; operand X's
+// element (row, col) is X[off_X(row) + col * inner_X] where off_X(row)
+// decodes `row` over the leading collapsed dims. A CTA handles TR rows per
+// tile: thread t < TR resolves row t's offsets into shared memory, then the
+// CTA streams the TR*L tile elements.
+// ---------------------------------------------------------------------------
+constexpr int kTileRowsMax = 256;
+
+struct BcastDesc {
+    int lead_rank;                      // collapsed leading dims (row decode)
+    std::size_t lead_dims[kMaxRank];
+    long long a_lead[kMaxRank];         // per-dim element strides
+    long long b_lead[kMaxRank];
+    long long a_inner, b_inner;         // stride along the row (0 or any)
+    std::size_t rows, L;
+    unsigned tile_rows;
+    FastDiv div_L;
+};
+
+template <int OP, bool VEC>
+__global__ void __launch_bounds__(kThreads)
+binary_tiled_kernel(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ out,
+                    const BcastDesc d, const float* __restrict__ sa, const float* __restrict__ sb,
+                    float av, float bv) {
+    __shared__ long long s_aoff[kTileRowsMax];
+    __shared__ long long s_boff[kTileRowsMax];
+    // A by-value operand is encoded as a null pointer with all strides 0.
+    const float a_const = sa ? __ldg(sa) : av;
+    const float b_const = sb ? __ldg(sb) : bv;
+    const std::size_t tiles = (d.rows + d.tile_rows - 1) / d.tile_rows;
+    for (std::size_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+        const std::size_t row0 = tile * d.tile_rows;
+        const unsigned nrows = static_cast<unsigned>(min(static_cast<std::size_t>(d.tile_rows), d.rows - row0));
+        if (threadIdx.x < nrows) {
+            std::size_t r = row0 + threadIdx.x;
+            long long ao = 0, bo = 0;
+            for (int k = d.lead_rank - 1; k >= 0; --k) {
+                const std::size_t dim = d.lead_dims[k];
+                const std::size_t c = r % dim;
+                r /= dim;
+                ao += static_cast<long long>(c) * d.a_lead[k];
+                bo += static_cast<long long>(c) * d.b_lead[k];
+            }
+            s_aoff[threadIdx.x] = ao;
+            s_boff[threadIdx.x] = bo;
+        }
+        __syncthreads();
+        const unsigned tile_elems = nrows * static_cast<unsigned>(d.L);
+        float* tile_out = out + row0 * d.L;
+        if constexpr (VEC) {
+            for (unsigned e = threadIdx.x * 4; e < tile_elems; e += kThreads * 4) {
+                unsigned row, col;
+                d.div_L.divmod(e, row, col);
+                float4 x, y;
+                if (!a) x = make_float4(a_const, a_const, a_const, a_const);
+                else if (d.a_inner == 0) { const float v = __ldg(a + s_aoff[row]); x = make_float4(v, v, v, v); }
+                else x = ldg4(a + s_aoff[row] + col);
+                if (!b) y = make_float4(b_const, b_const, b_const, b_const);
+                else if (d.b_inner == 0) { const float v = __ldg(b + s_boff[row]); y = make_float4(v, v, v, v); }
+                else y = ldg4(b + s_boff[row] + col);
+                st4_stream(tile_out + e, bop4<OP>(x, y));
+            }
+        } else {
+            for (unsigned e = threadIdx.x; e < tile_elems; e += kThreads) {
+                unsigned row, col;
+                d.div_L.divmod(e, row, col);
+                const float x = a ? __ldg(a + s_aoff[row] + static_cast<long long>(col) * d.a_inner) : a_const;
+                const float y = b ? __ldg(b + s_boff[row] + static_cast<long long>(col) * d.b_inner) : b_const;
+                tile_out[e] = bop<OP>(x, y);
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Unary and unary-backward flat kernels.
+// ---------------------------------------------------------------------------
+template <int OP, bool VEC>
+__global__ void __launch_bounds__(kThreads)
+unary_kernel(const float* __restrict__ in, float* __restrict__ out, std::size_t n) {
+    const std::size_t tid = static_cast<std::size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const std::size_t stride = static_cast<std::size_t>(gridDim.x) * blockDim.x;
+    if constexpr (VEC) {
+        const std::size_t n4 = n >> 2;
+        std::size_t i = tid;
+        for (; i + (kUnroll - 1) * stride < n4; i += kUnroll * stride) {
+            float4 x[kUnroll];
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) x[u] = ld4_stream(in + (i + u * stride) * 4);
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u)
+                st4_stream(out + (i + u * stride) * 4,
+                           make_float4(uop<OP>(x[u].x), uop<OP>(x[u].y), uop<OP>(x[u].z), uop<OP>(x[u].w)));
+        }
+        for (; i < n4; i += stride) {
+            const float4 x = ld4_stream(in + i * 4);
+            st4_stream(out + i * 4, make_float4(uop<OP>(x.x), uop<OP>(x.y), uop<OP>(x.z), uop<OP>(x.w)));
+        }
+        for (std::size_t k = n4 * 4 + tid; k < n; k += stride) out[k] = uop<OP>(in[k]);
+    } else {
+        for (std::size_t k = tid; k < n; k += stride) out[k] = uop<OP>(in[k]);
+    }
+}
+
+// Reads only the operands the rule needs (NEED_X / NEED_Y).
+template <int OP, bool VEC>
+__global__ void __launch_bounds__(kThreads)
+unary_backward_kernel(const float* __restrict__ x, const float* __restrict__ y,
+                      const float* __restrict__ g, float* __restrict__ dx, std::size_t n) {
+    constexpr bool NEED_X = OP == VC_LOG || OP == VC_RELU;
+    constexpr bool NEED_Y = OP == VC_EXP || OP == VC_SIGMOID;
+    const std::size_t tid = static_cast<std::size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const std::size_t stride = static_cast<std::size_t>(gridDim.x) * blockDim.x;
+    if constexpr (VEC) {
+        const std::size_t n4 = n >> 2;
+        std::size_t i = tid;
+        const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (; i + (kUnroll - 1) * stride < n4; i += kUnroll * stride) {
+            float4 gx[kUnroll], xx[kUnroll], yy[kUnroll];
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const std::size_t k = (i + u * stride) * 4;
+                gx[u] = ld4_stream(g + k);
+                xx[u] = NEED_X ? ld4_stream(x + k) : z;
+                yy[u] = NEED_Y ? ld4_stream(y + k) : z;
+            }
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u)
+                st4_stream(dx + (i + u * stride) * 4,
+                           make_float4(ubwd<OP>(xx[u].x, yy[u].x, gx[u].x), ubwd<OP>(xx[u].y, yy[u].y, gx[u].y),
+                                       ubwd<OP>(xx[u].z, yy[u].z, gx[u].z), ubwd<OP>(xx[u].w, yy[u].w, gx[u].w)));
+        }
+        for (; i < n4; i += stride) {
+            const std::size_t k = i * 4;
+            const float4 gv = ld4_stream(g + k);
+            const float4 xv = NEED_X ? ld4_stream(x + k) : z;
+            const float4 yv = NEED_Y ? ld4_stream(y + k) : z;
+            st4_stream(dx + k, make_float4(ubwd<OP>(xv.x, yv.x, gv.x), ubwd<OP>(xv.y, yv.y, gv.y),
+                                           ubwd<OP>(xv.z, yv.z, gv.z), ubwd<OP>(xv.w, yv.w, gv.w)));
+        }
+        for (std::size_t k = n4 * 4 + tid; k < n; k += stride)
+            dx[k] = ubwd<OP>(NEED_X ? x[k] : 0.f, NEED_Y ? y[k] : 0.f, g[k]);
+    } else {
+        for (std::size_t k = tid; k < n; k += stride)
+            dx[k] = ubwd<OP>(NEED_X ? x[k] : 0.f, NEED_Y ? y[k] : 0.f, g[k]);
+    }
+}
+
+__global__ void __launch_bounds__(kThreads)
+fill_kernel(float* __restrict__ out, std::size_t n, float value) {
+    const std::size_t stride = static_cast<std::size_t>(gridDim.x) * blockDim.x;
+    for (std::size_t k = static_cast<std::size_t>(blockIdx.x) * blockDim.x + threadIdx.x; k < n; k += stride)
+        out[k] = value;
+}
+
+__global__ void __launch_bounds__(kThreads)
+axpy_kernel(float* __restrict__ t, const float* __restrict__ s, std::size_t n, float alpha) {
+    const std::size_t stride = static_cast<std::size_t>(gridDim.x) * blockDim.x;
+    for (std::size_t k = static_cast<std::size_t>(blockIdx.x) * blockDim.x + threadIdx.x; k < n; k += stride)
+        t[k] = t[k] + alpha * s[k];
+}
+
+// ---------------------------------------------------------------------------
+// Host side: canonicalise a broadcast and pick a path.
+// ---------------------------------------------------------------------------
+struct Operand {
+    const float* ptr{nullptr};  // null: by-value constant
+    float value{0.0f};
+    long long strides[kMaxRank]{};  // aligned to the output dims; 0 = broadcast
+};
+
+// Align an operand of `shape` (contiguous, or with `strides`) to the output.
+static Operand align_operand(const float* ptr, const size_t* shape, const size_t* strides, int rank,
+                             const size_t* out_shape, int out_rank, const char* what) {
+    Operand op;
+    op.ptr = ptr;
+    if (rank > out_rank) fail(VC_ERR_INVALID, std::string(what) + ": operand rank exceeds the output rank");
+    std::size_t contiguous = 1;
+    for (int i = rank - 1; i >= 0; --i) {
+        const int o = i + (out_rank - rank);
+        const std::size_t dim = shape[i];
+        if (dim != out_shape[o] && dim != 1)
+            fail(VC_ERR_INVALID, std::string(what) + ": cannot broadcast operand to the output shape");
+        const std::size_t st = strides ? strides[i] : contiguous;
+        op.strides[o] = dim == 1 ? 0 : static_cast<long long>(st);
+        contiguous *= dim;
+    }
+    return op;
+}
+
+struct Canon {
+    int rank{0};
+    std::size_t dims[kMaxRank]{};
+    long long sa[kMaxRank]{};
+    long long sb[kMaxRank]{};
+};
+
+// Drop size-1 output dims and merge neighbours that are contiguous for both
+// operands (or broadcast in both).
+static Canon canonicalise(const size_t* out_shape, int out_rank, const Operand& a, const Operand& b) {
+    Canon c;
+    for (int i = 0; i < out_rank; ++i) {
+        if (out_shape[i] == 1) continue;
+        c.dims[c.rank] = out_shape[i];
+        c.sa[c.rank] = a.strides[i];
+        c.sb[c.rank] = b.strides[i];
+        ++c.rank;
+    }
+    Canon m;
+    for (int i = 0; i < c.rank; ++i) {
+        if (m.rank > 0) {
+            const int j = m.rank - 1;
+            const long long d = static_cast<long long>(c.dims[i]);
+            if (m.sa[j] == c.sa[i] * d && m.sb[j] == c.sb[i] * d) {
+                m.dims[j] *= c.dims[i];
+                m.sa[j] = c.sa[i];
+                m.sb[j] = c.sb[i];
+                continue;
+            }
+        }
+        m.dims[m.rank] = c.dims[i];
+        m.sa[m.rank] = c.sa[i];
+        m.sb[m.rank] = c.sb[i];
+        ++m.rank;
+    }
+    return m;
+}
+
+template <int OP>
+static void launch_binary_op(const Operand& a, const Operand& b, float* out, const Canon& c, std::size_t n) {
+    cudaStream_t s = stream();
+    const bool a_flat = c.rank <= 1 && (c.rank == 0 || c.sa[0] == 1);
+    const bool b_flat = c.rank <= 1 && (c.rank == 0 || c.sb[0] == 1);
+    const bool a_scalar = c.rank == 0 || (c.rank == 1 && c.sa[0] == 0);
+    const bool b_scalar = c.rank == 0 || (c.rank == 1 && c.sb[0] == 0);
+    int mode = -1;
+    if (a.ptr && b.ptr && a_flat && b_flat) mode = 0;
+    else if (a.ptr && a_flat && b_scalar) mode = 1;
+    else if (b.ptr && b_flat && a_scalar) mode = 2;
+    if (mode >= 0) {
+        const bool vec = aligned16(out) && (mode == 2 || aligned16(a.ptr)) && (mode == 1 || aligned16(b.ptr));
+        const unsigned grid = grid_for(vec ? (n + 3) / 4 : n, kThreads);
+        const float* sp = mode == 1 ? b.ptr : (mode == 2 ? a.ptr : nullptr);
+        const float sv = mode == 1 ? b.value : a.value;
+#define VC_FLAT(M, V) binary_flat_kernel<OP, M, V><<<grid, kThreads, 0, s>>>(a.ptr, b.ptr, out, n, sp, sv)
+        if (mode == 0) { if (vec) VC_FLAT(0, true); else VC_FLAT(0, false); }
+        else if (mode == 1) { if (vec) VC_FLAT(1, true); else VC_FLAT(1, false); }
+        else { if (vec) VC_FLAT(2, true); else VC_FLAT(2, false); }
+#undef VC_FLAT
+        check_launch("binary_flat");
+        return;
+    }
+    // Tiled strided path.
+    BcastDesc d{};
+    const int r = c.rank;  // >= 1 here
+    d.L = c.dims[r - 1];
+    d.a_inner = c.sa[r - 1];
+    d.b_inner = c.sb[r - 1];
+    d.lead_rank = r - 1;
+    d.rows = 1;
+    for (int i = 0; i < r - 1; ++i) {
+        d.lead_dims[i] = c.dims[i];
+        d.a_lead[i] = c.sa[i];
+        d.b_lead[i] = c.sb[i];
+        d.rows *= c.dims[i];
+    }
+    if (d.L > (1u << 30)) fail(VC_ERR_OVERFLOW, "broadcast inner run longer than 2^30 elements");
+    const std::size_t want = std::max<std::size_t>(1, 4096 / d.L);
+    d.tile_rows = static_cast<unsigned>(std::min<std::size_t>({want, static_cast<std::size_t>(kTileRowsMax), d.rows}));
+    d.div_L = FastDiv(static_cast<unsigned>(d.L));
+    auto lead_ok = [&](const long long* lead, long long inner, const float* p) {
+        if (!p || inner == 0) return true;
+        if (inner != 1 || !aligned16(p)) return false;
+        for (int i = 0; i < d.lead_rank; ++i)
+            if (lead[i] % 4) return false;
+        return true;
+    };
+    const bool vec = d.L % 4 == 0 && aligned16(out) && lead_ok(d.a_lead, d.a_inner, a.ptr) &&
+                     lead_ok(d.b_lead, d.b_inner, b.ptr);
+    const std::size_t tiles = (d.rows + d.tile_rows - 1) / d.tile_rows;
+    const unsigned grid = static_cast<unsigned>(std::min<std::size_t>(tiles, static_cast<std::size_t>(sm_count()) * 8));
+    if (vec) binary_tiled_kernel<OP, true><<<grid, kThreads, 0, s>>>(a.ptr, b.ptr, out, d, nullptr, nullptr, a.value, b.value);
+    else binary_tiled_kernel<OP, false><<<grid, kThreads, 0, s>>>(a.ptr, b.ptr, out, d, nullptr, nullptr, a.value, b.value);
+    check_launch("binary_tiled");
+}
+
+static void launch_binary(int op, const Operand& a, const Operand& b, float* out,
+                          const size_t* out_shape, int out_rank) {
+    const std::size_t n = checked_numel(out_shape, out_rank);
+    if (n == 0) return;
+    if (!out) fail(VC_ERR_INVALID, "binary: null output");
+    const Canon c = canonicalise(out_shape, out_rank, a, b);
+    switch (op) {
+        case VC_ADD: return launch_binary_op<VC_ADD>(a, b, out, c, n);
+        case VC_SUB: return launch_binary_op<VC_SUB>(a, b, out, c, n);
+        case VC_MUL: return launch_binary_op<VC_MUL>(a, b, out, c, n);
+        case VC_DIV: return launch_binary_op<VC_DIV>(a, b, out, c, n);
+        default: fail(VC_ERR_INVALID, "unknown binary operation");
+    }
+}
+
+template <int OP>
+static void launch_unary_op(const float* in, float* out, std::size_t n) {
+    const bool vec = aligned16(in) && aligned16(out);
+    const unsigned grid = grid_for(vec ? (n + 3) / 4 : n, kThreads);
+    if (vec) unary_kernel<OP, true><<<grid, kThreads, 0, stream()>>>(in, out, n);
+    else unary_kernel<OP, false><<<grid, kThreads, 0, stream()>>>(in, out, n);
+    check_launch("unary");
+}
+
+template <int OP>
+static void launch_unary_backward_op(const float* x, const float* y, const float* g, float* dx, std::size_t n) {
+    constexpr bool NEED_X = OP == VC_LOG || OP == VC_RELU;
+    constexpr bool NEED_Y = OP == VC_EXP || OP == VC_SIGMOID;
+    if ((NEED_X && !x) || (NEED_Y && !y)) fail(VC_ERR_INVALID, "unary_backward: the saved tensor this rule needs is null");
+    const bool vec = aligned16(g) && aligned16(dx) && (!NEED_X || aligned16(x)) && (!NEED_Y || aligned16(y));
+    const unsigned grid = grid_for(vec ? (n + 3) / 4 : n, kThreads);
+    if (vec) unary_backward_kernel<OP, true><<<grid, kThreads, 0, stream()>>>(x, y, g, dx, n);
+    else unary_backward_kernel<OP, false><<<grid, kThreads, 0, stream()>>>(x, y, g, dx, n);
+    check_launch("unary_backward");
+}
+
+}  // namespace vc
+
+using namespace vc;
+
+extern "C" {
+
+vc_status vc_cuda_binary(int op, const float* a, const size_t* a_shape, const size_t* a_strides, int a_rank,
+                         const float* b, const size_t* b_shape, const size_t* b_strides, int b_rank,
+                         float* out, const size_t* out_shape, int out_rank) {
+    VC_API_BEGIN
+    ensure_init();
+    validate_rank(a_rank, "binary");
+    validate_rank(b_rank, "binary");
+    validate_rank(out_rank, "binary");
+    if (op < VC_ADD || op > VC_DIV) fail(VC_ERR_INVALID, "unknown binary operation");
+    if (checked_numel(out_shape, out_rank) == 0) return VC_OK;
+    if (!a || !b) fail(VC_ERR_INVALID, "binary: null operand");
+    const Operand oa = align_operand(a, a_shape, a_strides, a_rank, out_shape, out_rank, "binary");
+    const Operand ob = align_operand(b, b_shape, b_strides, b_rank, out_shape, out_rank, "binary");
+    launch_binary(op, oa, ob, out, out_shape, out_rank);
+    VC_API_END
+}
+
+vc_status vc_cuda_binary_scalar(int op, const float* a, float scalar, int scalar_first, float* out,
+                                size_t count) {
+    VC_API_BEGIN
+    ensure_init();
+    if (op < VC_ADD || op > VC_DIV) fail(VC_ERR_INVALID, "unknown binary operation");
+    if (!count) return VC_OK;
+    if (!a || !out) fail(VC_ERR_INVALID, "binary_scalar: null pointer");
+    Operand t, s;
+    t.ptr = a;
+    t.strides[0] = 1;
+    s.ptr = nullptr;
+    s.value = scalar;
+    const size_t shape[1] = {count};
+    if (scalar_first) launch_binary(op, s, t, out, shape, 1);
+    else launch_binary(op, t, s, out, shape, 1);
+    VC_API_END
+}
+
+vc_status vc_cuda_unary(int op, const float* in, float* out, size_t count) {
+    VC_API_BEGIN
+    ensure_init();
+    if (!count) return VC_OK;
+    if (!in || !out) fail(VC_ERR_INVALID, "unary: null pointer");
+    switch (op) {
+        case VC_NEG: launch_unary_op<VC_NEG>(in, out, count); break;
+        case VC_RELU: launch_unary_op<VC_RELU>(in, out, count); break;
+        case VC_SIGMOID: launch_unary_op<VC_SIGMOID>(in, out, count); break;
+        case VC_RELU_GRAD: launch_unary_op<VC_RELU_GRAD>(in, out, count); break;
+        case VC_EXP: launch_unary_op<VC_EXP>(in, out, count); break;
+        case VC_LOG: launch_unary_op<VC_LOG>(in, out, count); break;
+        default: fail(VC_ERR_INVALID, "unknown unary operation");
+    }
+    VC_API_END
+}
+
+vc_status vc_cuda_unary_backward(int op, const float* x, const float* y, const float* g, float* dx,
+                                 size_t count) {
+    VC_API_BEGIN
+    ensure_init();
+    if (!count) return VC_OK;
+    if (!g || !dx) fail(VC_ERR_INVALID, "unary_backward: null pointer");
+    switch (op) {
+        case VC_NEG: launch_unary_backward_op<VC_NEG>(x, y, g, dx, count); break;
+        case VC_RELU: launch_unary_backward_op<VC_RELU>(x, y, g, dx, count); break;
+        case VC_SIGMOID: launch_unary_backward_op<VC_SIGMOID>(x, y, g, dx, count); break;
+        case VC_EXP: launch_unary_backward_op<VC_EXP>(x, y, g, dx, count); break;
+        case VC_LOG: launch_unary_backward_op<VC_LOG>(x, y, g, dx, count); break;
+        default: fail(VC_ERR_INVALID, "unary_backward: operation has no backward rule");
+    }
+    VC_API_END
+}
+
+vc_status vc_cuda_broadcast_to(const float* value, const size_t* v_shape, int v_rank, float* out,
+                               const size_t* t_shape, int t_rank) {
+    VC_API_BEGIN
+    ensure_init();
+    validate_rank(v_rank, "broadcast_to");
+    validate_rank(t_rank, "broadcast_to");
+    if (checked_numel(t_shape, t_rank) == 0) return VC_OK;
+    if (!value) fail(VC_ERR_INVALID, "broadcast_to: null value");
+    const Operand ov = align_operand(value, v_shape, nullptr, v_rank, t_shape, t_rank, "broadcast_to");
+    Operand zero;  // by-value 0.0f: value + 0 turns -0 into +0 like the reference
+    launch_binary(VC_ADD, ov, zero, out, t_shape, t_rank);
+    VC_API_END
+}
+
+vc_status vc_cuda_fill(float* out, size_t count, float value) {
+    VC_API_BEGIN
+    ensure_init();
+    if (!count) return VC_OK;
+    fill_kernel<<<grid_for(count, kThreads), kThreads, 0, stream()>>>(out, count, value);
+    check_launch("fill");
+    VC_API_END
+}
+
+vc_status vc_cuda_axpy(float* target, const float* source, size_t count, float alpha) {
+    VC_API_BEGIN
+    ensure_init();
+    if (!count) return VC_OK;
+    if (!target || !source) fail(VC_ERR_INVALID, "axpy: null pointer");
+    axpy_kernel<<<grid_for(count, kThreads), kThreads, 0, stream()>>>(target, source, count, alpha);
+    check_launch("axpy");
+    VC_API_END
+}
+
+}  // extern "C"

@@ -1,0 +1,869 @@
+// reduce.cu -- deterministic reductions for sm_100a:
+//   * the fused broadcast-gradient reduction (sum_to_shape) and the fused
+//     backward rules of the binary ops, which compute g*b, g/b, -(g*a)/(b*b)
+//     per element and reduce over every broadcast axis in ONE pass (the
+//     reference runs one full pass per axis plus a temporary per product,
+//     src/autograd.cpp:50-72, src/ops.cpp:98-156);
+//   * full and per-axis sum / mean (cpu::sum, cpu::reduce_axis);
+//   * per-axis and full max / argmax with the reference's strict '>' scan
+//     semantics, and their fused backward (scatter) passes.
+//
+// Every kernel streams its input once from HBM. Sums accumulate in double and
+// round to float once (the reference accumulates in double, cpu_backend.cpp
+// :392-418, :434-441). The work split -- segments of the reduced index space,
+// each producing a partial in stream-ordered scratch, combined in segment
+// order by a second kernel -- is derived from the shapes only (never from the
+// SM count), so results do not depend on the launch configuration.
+#include "vc_internal.cuh"
+
+#include <algorithm>
+#include <cstring>
+
+namespace vc {
+
+namespace {
+
+constexpr unsigned kThreads = 256;
+// Aim for about this many threads of work before splitting a reduction into
+// segments (a constant, so the split depends on the problem size alone).
+constexpr unsigned long long kTargetThreads = 1ull << 18;
+constexpr unsigned long long kMinSegment = 16;         // reduced positions per segment (column)
+constexpr unsigned long long kRowChunk = 1ull << 16;   // elements per segment (row)
+
+// Element functions of the backward rules, arithmetic exactly as written in
+// src/ops.cpp: p, q are the other operands broadcast to the output shape.
+enum Vjp { V_G = 0, V_NEG = 1, V_MUL = 2, V_DIV_A = 3, V_DIV_B = 4 };
+
+template <int F>
+__device__ __forceinline__ float vjp(float g, float p, float q) {
+    if constexpr (F == V_G) return g;
+    else if constexpr (F == V_NEG) return -g;
+    else if constexpr (F == V_MUL) return g * p;
+    else if constexpr (F == V_DIV_A) return g / p;
+    else {  // -(gradient * a) / (b * b)
+        const float ga = g * p;
+        const float neg = -ga;
+        const float bb = q * q;
+        return neg / bb;
+    }
+}
+
+template <int F> __host__ __device__ constexpr int operands() { return F == V_G || F == V_NEG ? 1 : (F == V_DIV_B ? 3 : 2); }
+
+// Canonical reduction layout. Dimensions of the source (forward output)
+// shape are classified kept / reduced and merged; operand 0 is g, 1 is p,
+// 2 is q. COLUMN layout: the innermost dim is kept (a run of `inner`
+// outputs). ROW layout: the innermost dim is reduced (a run of `inner`
+// reduced elements).
+struct RedDesc {
+    int nk;
+    unsigned long long kdims[kMaxRank];
+    long long ks[3][kMaxRank];
+    int nr;
+    unsigned long long rdims[kMaxRank];
+    long long rs[3][kMaxRank];
+    unsigned long long inner;
+    long long is[3];
+    unsigned long long K;   // kept-outer positions
+    unsigned long long R;   // reduced-outer positions (COLUMN: all reduced positions)
+    unsigned long long seg; // COLUMN: reduced positions per segment; ROW: elements per segment
+    unsigned S;             // segments
+    float divisor;          // mean: divide the rounded sum by this (0 = none)
+};
+
+__device__ __forceinline__ void decode(unsigned long long idx, int n, const unsigned long long* dims,
+                                       const long long (*st)[kMaxRank], long long off[3],
+                                       unsigned long long* coord) {
+    off[0] = off[1] = off[2] = 0;
+    for (int k = n - 1; k >= 0; --k) {
+        const unsigned long long c = idx % dims[k];
+        idx /= dims[k];
+        if (coord) coord[k] = c;
+        off[0] += static_cast<long long>(c) * st[0][k];
+        off[1] += static_cast<long long>(c) * st[1][k];
+        off[2] += static_cast<long long>(c) * st[2][k];
+    }
+}
+
+__device__ __forceinline__ float4 load4(const float* base, long long off, long long inner_stride,
+                                        unsigned long long i) {
+    if (inner_stride == 0) {
+        const float v = __ldg(base + off);
+        return make_float4(v, v, v, v);
+    }
+    return ldg4(base + off + static_cast<long long>(i));
+}
+
+__device__ __forceinline__ float round_out(double acc, float divisor) {
+    const float s = static_cast<float>(acc);
+    return divisor != 0.0f ? s / divisor : s;
+}
+
+// ---------------------------------------------------------------------------
+// COLUMN layout. grid = (ceil(inner / (256*V)), min(K, 65535), S).
+// ---------------------------------------------------------------------------
+template <int F, bool VEC>
+__global__ void __launch_bounds__(kThreads)
+reduce_col_kernel(const float* __restrict__ g, const float* __restrict__ p, const float* __restrict__ q,
+                  const RedDesc d, float* __restrict__ out, double* __restrict__ partial) {
+    constexpr int V = VEC ? 4 : 1;
+    constexpr int NOPS = operands<F>();
+    const unsigned long long i0 = (static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x) * V;
+    if (i0 >= d.inner) return;
+    const unsigned s = blockIdx.z;
+    const unsigned long long r0 = s * d.seg;
+    const unsigned long long r1 = min(d.R, r0 + d.seg);
+    for (unsigned long long ko = blockIdx.y; ko < d.K; ko += gridDim.y) {
+        long long base[3];
+        decode(ko, d.nk, d.kdims, d.ks, base, nullptr);
+        long long off[3];
+        unsigned long long coord[kMaxRank];
+        decode(r0, d.nr, d.rdims, d.rs, off, coord);
+        double acc[V];
+#pragma unroll
+        for (int v = 0; v < V; ++v) acc[v] = 0.0;
+        for (unsigned long long r = r0; r < r1; ++r) {
+            if constexpr (VEC) {
+                const float4 gv = load4(g, base[0] + off[0], d.is[0], i0);
+                const float4 pv = NOPS > 1 ? load4(p, base[1] + off[1], d.is[1], i0) : gv;
+                const float4 qv = NOPS > 2 ? load4(q, base[2] + off[2], d.is[2], i0) : gv;
+                acc[0] += vjp<F>(gv.x, pv.x, qv.x);
+                acc[1] += vjp<F>(gv.y, pv.y, qv.y);
+                acc[2] += vjp<F>(gv.z, pv.z, qv.z);
+                acc[3] += vjp<F>(gv.w, pv.w, qv.w);
+            } else {
+                const float gv = __ldg(g + base[0] + off[0] + static_cast<long long>(i0) * d.is[0]);
+                const float pv = NOPS > 1 ? __ldg(p + base[1] + off[1] + static_cast<long long>(i0) * d.is[1]) : gv;
+                const float qv = NOPS > 2 ? __ldg(q + base[2] + off[2] + static_cast<long long>(i0) * d.is[2]) : gv;
+                acc[0] += vjp<F>(gv, pv, qv);
+            }
+            // advance the reduced coordinate (row-major carry)
+            for (int k = d.nr - 1; k >= 0; --k) {
+                off[0] += d.rs[0][k];
+                off[1] += d.rs[1][k];
+                off[2] += d.rs[2][k];
+                if (++coord[k] < d.rdims[k]) break;
+                coord[k] = 0;
+                off[0] -= d.rs[0][k] * static_cast<long long>(d.rdims[k]);
+                off[1] -= d.rs[1][k] * static_cast<long long>(d.rdims[k]);
+                off[2] -= d.rs[2][k] * static_cast<long long>(d.rdims[k]);
+            }
+        }
+        const unsigned long long o = ko * d.inner + i0;
+        if (d.S == 1) {
+            if constexpr (VEC)
+                st4(out + o, make_float4(round_out(acc[0], d.divisor), round_out(acc[1], d.divisor),
+                                         round_out(acc[2], d.divisor), round_out(acc[3], d.divisor)));
+            else out[o] = round_out(acc[0], d.divisor);
+        } else {
+            double* dst = partial + static_cast<unsigned long long>(s) * d.K * d.inner + o;
+#pragma unroll
+            for (int v = 0; v < V; ++v) dst[v] = acc[v];
+        }
+    }
+}
+
+// Combine COLUMN partials [S][K*inner] in segment order.
+__global__ void __launch_bounds__(kThreads)
+reduce_col_finish(const double* __restrict__ partial, unsigned S, unsigned long long count,
+                  float divisor, float* __restrict__ out) {
+    const unsigned long long stride = static_cast<unsigned long long>(gridDim.x) * blockDim.x;
+    for (unsigned long long o = static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x; o < count;
+         o += stride) {
+        double acc = 0.0;
+        for (unsigned s = 0; s < S; ++s) acc += partial[static_cast<unsigned long long>(s) * count + o];
+        out[o] = round_out(acc, divisor);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// ROW layout. Each output k reduces W = R * inner elements (e = r*inner + l).
+// grid = (min(K, 65535) rows, S segments of d.seg elements).
+// ---------------------------------------------------------------------------
+template <int F, bool VEC, bool HAS_R>
+__global__ void __launch_bounds__(kThreads)
+reduce_row_kernel(const float* __restrict__ g, const float* __restrict__ p, const float* __restrict__ q,
+                  const RedDesc d, float* __restrict__ out, double* __restrict__ partial) {
+    constexpr int V = VEC ? 4 : 1;
+    constexpr int NOPS = operands<F>();
+    __shared__ double s_red[32];
+    const unsigned long long W = d.R * d.inner;
+    const unsigned s = blockIdx.y;
+    const unsigned long long e0 = s * d.seg;
+    const unsigned long long e1 = min(W, e0 + d.seg);
+    for (unsigned long long k = blockIdx.x; k < d.K; k += gridDim.x) {
+        long long base[3];
+        decode(k, d.nk, d.kdims, d.ks, base, nullptr);
+        double acc0 = 0.0, acc1 = 0.0;
+        for (unsigned long long e = e0 + threadIdx.x * V; e < e1; e += kThreads * V) {
+            long long off[3] = {0, 0, 0};
+            unsigned long long l = e;
+            if constexpr (HAS_R) {
+                const unsigned long long r = e / d.inner;
+                l = e - r * d.inner;
+                decode(r, d.nr, d.rdims, d.rs, off, nullptr);
+            }
+            if constexpr (VEC) {
+                const float4 gv = load4(g, base[0] + off[0], d.is[0], l);
+                const float4 pv = NOPS > 1 ? load4(p, base[1] + off[1], d.is[1], l) : gv;
+                const float4 qv = NOPS > 2 ? load4(q, base[2] + off[2], d.is[2], l) : gv;
+                acc0 += static_cast<double>(vjp<F>(gv.x, pv.x, qv.x)) + static_cast<double>(vjp<F>(gv.y, pv.y, qv.y));
+                acc1 += static_cast<double>(vjp<F>(gv.z, pv.z, qv.z)) + static_cast<double>(vjp<F>(gv.w, pv.w, qv.w));
+            } else {
+                const long long li = static_cast<long long>(l);
+                const float gv = __ldg(g + base[0] + off[0] + li * d.is[0]);
+                const float pv = NOPS > 1 ? __ldg(p + base[1] + off[1] + li * d.is[1]) : gv;
+                const float qv = NOPS > 2 ? __ldg(q + base[2] + off[2] + li * d.is[2]) : gv;
+                acc0 += vjp<F>(gv, pv, qv);
+            }
+        }
+        const double total = block_sum(acc0 + acc1, s_red);
+        if (threadIdx.x == 0) {
+            if (d.S == 1) out[k] = round_out(total, d.divisor);
+            else partial[k * d.S + s] = total;
+        }
+        __syncthreads();
+    }
+}
+
+// Combine ROW partials [K][S] in segment order.
+__global__ void __launch_bounds__(kThreads)
+reduce_row_finish(const double* __restrict__ partial, unsigned S, unsigned long long K, float divisor,
+                  float* __restrict__ out) {
+    const unsigned long long stride = static_cast<unsigned long long>(gridDim.x) * blockDim.x;
+    for (unsigned long long k = static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x; k < K;
+         k += stride) {
+        double acc = 0.0;
+        for (unsigned s = 0; s < S; ++s) acc += partial[k * S + s];
+        out[k] = round_out(acc, divisor);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Host: build the canonical layout and launch.
+// ---------------------------------------------------------------------------
+struct Src {
+    const float* ptr{nullptr};
+    long long st[kMaxRank]{};  // aligned to the source dims
+};
+
+// Strides of a contiguous operand of `shape` aligned to the source shape.
+static Src align(const float* ptr, const size_t* shape, int rank, const size_t* src_shape, int src_rank,
+                 const char* what) {
+    Src s;
+    s.ptr = ptr;
+    if (rank > src_rank) fail(VC_ERR_INVALID, std::string(what) + ": operand rank exceeds the output rank");
+    long long contiguous = 1;
+    for (int i = rank - 1; i >= 0; --i) {
+        const int o = i + (src_rank - rank);
+        if (shape[i] != src_shape[o] && shape[i] != 1)
+            fail(VC_ERR_INVALID, std::string(what) + ": operand does not broadcast to the output shape");
+        s.st[o] = shape[i] == 1 ? 0 : contiguous;
+        contiguous *= static_cast<long long>(shape[i]);
+    }
+    return s;
+}
+
+template <int F>
+static void launch_vjp_reduce(const Src ops[3], const size_t* src_shape, int src_rank, const size_t* t_shape,
+                              int t_rank, float* out, float divisor) {
+    // 1. classify source dims: 0 drop (size 1), 1 kept, 2 reduced.
+    if (t_rank > src_rank) fail(VC_ERR_INVALID, "sum_to_shape: cannot reduce to a larger rank");
+    const int lead = src_rank - t_rank;
+    int cls[kMaxRank];
+    std::size_t outsz = 1;
+    for (int i = 0; i < src_rank; ++i) {
+        const std::size_t td = i < lead ? 1 : t_shape[i - lead];
+        const std::size_t sd = src_shape[i];
+        if (td != sd && td != 1) fail(VC_ERR_INVALID, "sum_to_shape: cannot reduce the gradient to the target shape");
+        cls[i] = sd == 1 ? 0 : (td == 1 ? 2 : 1);
+        if (cls[i] == 1) outsz *= sd;
+    }
+    // 2. merge neighbours of the same class that are contiguous for every operand.
+    struct Dim { int cls; unsigned long long size; long long st[3]; };
+    Dim dims[kMaxRank];
+    int nd = 0;
+    for (int i = 0; i < src_rank; ++i) {
+        if (cls[i] == 0) continue;
+        Dim cur{cls[i], src_shape[i], {ops[0].st[i], ops[1].st[i], ops[2].st[i]}};
+        if (nd > 0 && dims[nd - 1].cls == cur.cls) {
+            Dim& prev = dims[nd - 1];
+            bool ok = true;
+            for (int k = 0; k < 3; ++k)
+                ok = ok && prev.st[k] == cur.st[k] * static_cast<long long>(cur.size);
+            if (ok) {
+                prev.size *= cur.size;
+                for (int k = 0; k < 3; ++k) prev.st[k] = cur.st[k];
+                continue;
+            }
+        }
+        dims[nd++] = cur;
+    }
+    if (outsz == 0) return;
+    RedDesc d{};
+    d.divisor = divisor;
+    if (nd == 0 || dims[nd - 1].cls == 1) {
+        // COLUMN (also covers "nothing to reduce").
+        const unsigned long long inner = nd ? dims[nd - 1].size : 1;
+        d.inner = inner;
+        for (int k = 0; k < 3; ++k) d.is[k] = nd ? dims[nd - 1].st[k] : 0;
+        d.K = 1;
+        d.R = 1;
+        for (int i = 0; i + 1 < nd; ++i) {
+            if (dims[i].cls == 1) {
+                d.kdims[d.nk] = dims[i].size;
+                for (int k = 0; k < 3; ++k) d.ks[k][d.nk] = dims[i].st[k];
+                ++d.nk;
+                d.K *= dims[i].size;
+            } else {
+                d.rdims[d.nr] = dims[i].size;
+                for (int k = 0; k < 3; ++k) d.rs[k][d.nr] = dims[i].st[k];
+                ++d.nr;
+                d.R *= dims[i].size;
+            }
+        }
+        bool vec = inner % 4 == 0 && aligned16(out);
+        for (int k = 0; k < operands<F>(); ++k) {
+            if (d.is[k] == 0) continue;
+            if (d.is[k] != 1 || !aligned16(ops[k].ptr)) { vec = false; break; }
+            for (int i = 0; i < d.nk; ++i) vec = vec && d.ks[k][i] % 4 == 0;
+            for (int i = 0; i < d.nr; ++i) vec = vec && d.rs[k][i] % 4 == 0;
+        }
+        const unsigned V = vec ? 4 : 1;
+        const unsigned long long lanes = (inner + V - 1) / V;
+        const unsigned long long threads_now = lanes * d.K;
+        unsigned long long S = (kTargetThreads + threads_now - 1) / threads_now;
+        S = std::min<unsigned long long>(S, (d.R + kMinSegment - 1) / kMinSegment);
+        S = std::max<unsigned long long>(S, 1);
+        S = std::min<unsigned long long>(S, 4096);
+        d.seg = (d.R + S - 1) / S;
+        d.S = static_cast<unsigned>((d.R + d.seg - 1) / d.seg);
+        dim3 grid(static_cast<unsigned>((lanes + kThreads - 1) / kThreads),
+                  static_cast<unsigned>(std::min<unsigned long long>(d.K, 65535)), d.S);
+        if (grid.x > 0x7fffffffu) fail(VC_ERR_OVERFLOW, "reduction inner run too long");
+        Scratch partial(d.S > 1 ? static_cast<std::size_t>(d.S) * d.K * d.inner * sizeof(double) : 8);
+        if (vec) reduce_col_kernel<F, true><<<grid, kThreads, 0, stream()>>>(ops[0].ptr, ops[1].ptr, ops[2].ptr, d, out, partial.as<double>());
+        else reduce_col_kernel<F, false><<<grid, kThreads, 0, stream()>>>(ops[0].ptr, ops[1].ptr, ops[2].ptr, d, out, partial.as<double>());
+        check_launch("reduce_col");
+        if (d.S > 1) {
+            const unsigned long long count = d.K * d.inner;
+            reduce_col_finish<<<grid_for(count, kThreads), kThreads, 0, stream()>>>(partial.as<double>(), d.S, count, divisor, out);
+            check_launch("reduce_col_finish");
+        }
+        return;
+    }
+    // ROW: innermost reduced run.
+    const unsigned long long inner = dims[nd - 1].size;
+    d.inner = inner;
+    for (int k = 0; k < 3; ++k) d.is[k] = dims[nd - 1].st[k];
+    d.K = 1;
+    d.R = 1;
+    for (int i = 0; i + 1 < nd; ++i) {
+        if (dims[i].cls == 1) {
+            d.kdims[d.nk] = dims[i].size;
+            for (int k = 0; k < 3; ++k) d.ks[k][d.nk] = dims[i].st[k];
+            ++d.nk;
+            d.K *= dims[i].size;
+        } else {
+            d.rdims[d.nr] = dims[i].size;
+            for (int k = 0; k < 3; ++k) d.rs[k][d.nr] = dims[i].st[k];
+            ++d.nr;
+            d.R *= dims[i].size;
+        }
+    }
+    bool vec = inner % 4 == 0;
+    for (int k = 0; k < operands<F>(); ++k) {
+        if (d.is[k] == 0) continue;
+        if (d.is[k] != 1 || !aligned16(ops[k].ptr)) { vec = false; break; }
+        for (int i = 0; i < d.nk; ++i) vec = vec && d.ks[k][i] % 4 == 0;
+        for (int i = 0; i < d.nr; ++i) vec = vec && d.rs[k][i] % 4 == 0;
+    }
+    const unsigned long long W = d.R * d.inner;
+    unsigned long long S = (W + kRowChunk - 1) / kRowChunk;
+    S = std::max<unsigned long long>(S, 1);
+    S = std::min<unsigned long long>(S, 65535);
+    unsigned long long seg = (W + S - 1) / S;
+    seg = (seg + 3) / 4 * 4;  // keep float4 groups inside one segment
+    d.seg = seg;
+    d.S = static_cast<unsigned>((W + seg - 1) / seg);
+    dim3 grid(static_cast<unsigned>(std::min<unsigned long long>(d.K, 1u << 20)), d.S);
+    Scratch partial(d.S > 1 ? static_cast<std::size_t>(d.S) * d.K * sizeof(double) : 8);
+    const bool has_r = d.nr > 0;
+#define VC_ROW(V, H) reduce_row_kernel<F, V, H><<<grid, kThreads, 0, stream()>>>(ops[0].ptr, ops[1].ptr, ops[2].ptr, d, out, partial.as<double>())
+    if (vec) { if (has_r) VC_ROW(true, true); else VC_ROW(true, false); }
+    else { if (has_r) VC_ROW(false, true); else VC_ROW(false, false); }
+#undef VC_ROW
+    check_launch("reduce_row");
+    if (d.S > 1) {
+        reduce_row_finish<<<grid_for(d.K, kThreads), kThreads, 0, stream()>>>(partial.as<double>(), d.S, d.K, divisor, out);
+        check_launch("reduce_row_finish");
+    }
+}
+
+static void vjp_reduce(int f, const Src ops[3], const size_t* src_shape, int src_rank, const size_t* t_shape,
+                       int t_rank, float* out, float divisor = 0.0f) {
+    switch (f) {
+        case V_G: return launch_vjp_reduce<V_G>(ops, src_shape, src_rank, t_shape, t_rank, out, divisor);
+        case V_NEG: return launch_vjp_reduce<V_NEG>(ops, src_shape, src_rank, t_shape, t_rank, out, divisor);
+        case V_MUL: return launch_vjp_reduce<V_MUL>(ops, src_shape, src_rank, t_shape, t_rank, out, divisor);
+        case V_DIV_A: return launch_vjp_reduce<V_DIV_A>(ops, src_shape, src_rank, t_shape, t_rank, out, divisor);
+        default: return launch_vjp_reduce<V_DIV_B>(ops, src_shape, src_rank, t_shape, t_rank, out, divisor);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Same-shape binary backward: both gradients in one pass (20 B/elem for mul
+// and div: read g, a, b; write da, db).
+// ---------------------------------------------------------------------------
+template <int OP, bool VEC>
+__global__ void __launch_bounds__(kThreads)
+binary_backward_flat(const float* __restrict__ a, const float* __restrict__ b, const float* __restrict__ g,
+                     float* __restrict__ da, float* __restrict__ db, std::size_t n) {
+    const std::size_t stride = static_cast<std::size_t>(gridDim.x) * blockDim.x;
+    const std::size_t tid = static_cast<std::size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    auto one = [&](float av, float bv, float gv, float& ga, float& gb) {
+        if constexpr (OP == VC_ADD) { ga = gv; gb = gv; }
+        else if constexpr (OP == VC_SUB) { ga = gv; gb = -gv; }
+        else if constexpr (OP == VC_MUL) { ga = vjp<V_MUL>(gv, bv, 0.f); gb = vjp<V_MUL>(gv, av, 0.f); }
+        else { ga = vjp<V_DIV_A>(gv, bv, 0.f); gb = vjp<V_DIV_B>(gv, av, bv); }
+    };
+    constexpr bool NEED_A = OP == VC_MUL || OP == VC_DIV;
+    constexpr bool NEED_B = OP == VC_MUL || OP == VC_DIV;
+    if constexpr (VEC) {
+        const std::size_t n4 = n >> 2;
+        for (std::size_t i = tid; i < n4; i += stride) {
+            const std::size_t k = i * 4;
+            const float4 gv = ld4_stream(g + k);
+            const float4 av = NEED_A ? ld4_stream(a + k) : gv;
+            const float4 bv = NEED_B ? ld4_stream(b + k) : gv;
+            float4 ga, gb;
+            one(av.x, bv.x, gv.x, ga.x, gb.x);
+            one(av.y, bv.y, gv.y, ga.y, gb.y);
+            one(av.z, bv.z, gv.z, ga.z, gb.z);
+            one(av.w, bv.w, gv.w, ga.w, gb.w);
+            st4_stream(da + k, ga);
+            st4_stream(db + k, gb);
+        }
+        for (std::size_t k = n4 * 4 + tid; k < n; k += stride) one(NEED_A ? a[k] : 0.f, NEED_B ? b[k] : 0.f, g[k], da[k], db[k]);
+    } else {
+        for (std::size_t k = tid; k < n; k += stride) one(NEED_A ? a[k] : 0.f, NEED_B ? b[k] : 0.f, g[k], da[k], db[k]);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Max / argmax over [outer, length, inner] with the reference's scan
+// semantics (cpu_backend.cpp:443-453): a strictly larger value replaces the
+// best, so the first maximal index wins; NaN never replaces, so a NaN wins
+// only at index 0. Candidates exclude NaN; the finish step applies the
+// index-0 rule (unless `continuation`, used by later shards of a sharded
+// axis, which report -1 when they have no candidate).
+// ---------------------------------------------------------------------------
+struct MaxOut {
+    float* values;        // max value, or argmax as float (reference convention)
+    long long* index;     // int64 argmax (optional)
+    int argmax_as_value;  // write the index (as float) into values
+    int continuation;
+    long long index_base; // added to indices (shard offset)
+};
+
+__device__ __forceinline__ void max_finish_write(MaxCand c, float first, const MaxOut& o, unsigned long long k) {
+    if (!o.continuation && first != first) c = MaxCand{first, 0};  // NaN at index 0 wins
+    const long long idx = c.i < 0 ? -1 : c.i + o.index_base;
+    if (o.values) o.values[k] = o.argmax_as_value ? static_cast<float>(idx) : c.v;
+    if (o.index) o.index[k] = idx;
+}
+
+// ROW (inner == 1): grid = (rows, segments).
+template <bool VEC>
+__global__ void __launch_bounds__(kThreads)
+max_row_kernel(const float* __restrict__ in, unsigned long long outer, unsigned long long length,
+               unsigned long long seg, unsigned S, MaxOut o, float* __restrict__ pv, long long* __restrict__ pi) {
+    __shared__ float s_v[32];
+    __shared__ long long s_i[32];
+    const unsigned s = blockIdx.y;
+    const unsigned long long e0 = s * seg, e1 = min(length, e0 + seg);
+    for (unsigned long long row = blockIdx.x; row < outer; row += gridDim.x) {
+        const float* x = in + row * length;
+        MaxCand c{0.0f, -1};
+        if constexpr (VEC) {
+            for (unsigned long long e = e0 + threadIdx.x * 4; e < e1; e += kThreads * 4) {
+                const float4 v = ldg4(x + e);
+                c = max_take(c, v.x, static_cast<long long>(e));
+                c = max_take(c, v.y, static_cast<long long>(e + 1));
+                c = max_take(c, v.z, static_cast<long long>(e + 2));
+                c = max_take(c, v.w, static_cast<long long>(e + 3));
+            }
+        } else {
+            for (unsigned long long e = e0 + threadIdx.x; e < e1; e += kThreads)
+                c = max_take(c, __ldg(x + e), static_cast<long long>(e));
+        }
+        c = block_max(c, s_v, s_i);
+        if (threadIdx.x == 0) {
+            if (S == 1) max_finish_write(c, __ldg(x), o, row);
+            else { pv[row * S + s] = c.v; pi[row * S + s] = c.i; }
+        }
+        __syncthreads();
+    }
+}
+
+__global__ void __launch_bounds__(kThreads)
+max_row_finish(const float* __restrict__ in, unsigned long long outer, unsigned long long length, unsigned S,
+               const float* __restrict__ pv, const long long* __restrict__ pi, MaxOut o) {
+    const unsigned long long stride = static_cast<unsigned long long>(gridDim.x) * blockDim.x;
+    for (unsigned long long row = static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x; row < outer;
+         row += stride) {
+        MaxCand c{0.0f, -1};
+        for (unsigned s = 0; s < S; ++s) c = max_combine(c, MaxCand{pv[row * S + s], pi[row * S + s]});
+        max_finish_write(c, in[row * length], o, row);
+    }
+}
+
+// COLUMN (inner > 1): grid = (ceil(inner/256), min(outer, 65535), segments).
+__global__ void __launch_bounds__(kThreads)
+max_col_kernel(const float* __restrict__ in, unsigned long long outer, unsigned long long length,
+               unsigned long long inner, unsigned long long seg, unsigned S, MaxOut o,
+               float* __restrict__ pv, long long* __restrict__ pi) {
+    const unsigned long long i = static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= inner) return;
+    const unsigned s = blockIdx.z;
+    const unsigned long long a0 = s * seg, a1 = min(length, a0 + seg);
+    for (unsigned long long ob = blockIdx.y; ob < outer; ob += gridDim.y) {
+        const float* x = in + ob * length * inner + i;
+        MaxCand c{0.0f, -1};
+        for (unsigned long long a = a0; a < a1; ++a) c = max_take(c, __ldg(x + a * inner), static_cast<long long>(a));
+        const unsigned long long k = ob * inner + i;
+        if (S == 1) max_finish_write(c, __ldg(x), o, k);
+        else { pv[s * outer * inner + k] = c.v; pi[s * outer * inner + k] = c.i; }
+    }
+}
+
+__global__ void __launch_bounds__(kThreads)
+max_col_finish(const float* __restrict__ in, unsigned long long outer, unsigned long long length,
+               unsigned long long inner, unsigned S, const float* __restrict__ pv,
+               const long long* __restrict__ pi, MaxOut o) {
+    const unsigned long long count = outer * inner;
+    const unsigned long long stride = static_cast<unsigned long long>(gridDim.x) * blockDim.x;
+    for (unsigned long long k = static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x; k < count;
+         k += stride) {
+        MaxCand c{0.0f, -1};
+        for (unsigned s = 0; s < S; ++s) c = max_combine(c, MaxCand{pv[s * count + k], pi[s * count + k]});
+        const unsigned long long ob = k / inner, i = k - ob * inner;
+        max_finish_write(c, in[ob * length * inner + i], o, k);
+    }
+}
+
+static void launch_max(const float* in, std::size_t outer, std::size_t length, std::size_t inner, MaxOut o) {
+    if (outer * inner == 0) return;
+    if (length == 0) fail(VC_ERR_INVALID, "max/argmax over an empty axis is undefined");
+    cudaStream_t st = stream();
+    if (inner == 1) {
+        unsigned long long S = std::max<unsigned long long>(1, (length + kRowChunk - 1) / kRowChunk);
+        S = std::min<unsigned long long>(S, 65535);
+        unsigned long long seg = ((length + S - 1) / S + 3) / 4 * 4;
+        const unsigned Sn = static_cast<unsigned>((length + seg - 1) / seg);
+        const bool vec = aligned16(in) && length % 4 == 0;
+        Scratch pv(Sn > 1 ? outer * Sn * sizeof(float) : 8), pi(Sn > 1 ? outer * Sn * sizeof(long long) : 8);
+        dim3 grid(static_cast<unsigned>(std::min<std::size_t>(outer, 1u << 20)), Sn);
+        if (vec) max_row_kernel<true><<<grid, kThreads, 0, st>>>(in, outer, length, seg, Sn, o, pv.as<float>(), pi.as<long long>());
+        else max_row_kernel<false><<<grid, kThreads, 0, st>>>(in, outer, length, seg, Sn, o, pv.as<float>(), pi.as<long long>());
+        check_launch("max_row");
+        if (Sn > 1) {
+            max_row_finish<<<grid_for(outer, kThreads), kThreads, 0, st>>>(in, outer, length, Sn, pv.as<float>(), pi.as<long long>(), o);
+            check_launch("max_row_finish");
+        }
+        return;
+    }
+    const unsigned long long lanes = inner;
+    const unsigned long long threads_now = lanes * outer;
+    unsigned long long S = (kTargetThreads + threads_now - 1) / threads_now;
+    S = std::min<unsigned long long>(S, (length + kMinSegment - 1) / kMinSegment);
+    S = std::max<unsigned long long>(1, std::min<unsigned long long>(S, 4096));
+    const unsigned long long seg = (length + S - 1) / S;
+    const unsigned Sn = static_cast<unsigned>((length + seg - 1) / seg);
+    Scratch pv(Sn > 1 ? outer * inner * Sn * sizeof(float) : 8), pi(Sn > 1 ? outer * inner * Sn * sizeof(long long) : 8);
+    dim3 grid(static_cast<unsigned>((inner + kThreads - 1) / kThreads),
+              static_cast<unsigned>(std::min<std::size_t>(outer, 65535)), Sn);
+    max_col_kernel<<<grid, kThreads, 0, st>>>(in, outer, length, inner, seg, Sn, o, pv.as<float>(), pi.as<long long>());
+    check_launch("max_col");
+    if (Sn > 1) {
+        max_col_finish<<<grid_for(outer * inner, kThreads), kThreads, 0, st>>>(in, outer, length, inner, Sn, pv.as<float>(), pi.as<long long>(), o);
+        check_launch("max_col_finish");
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Backward of axis reductions, one write pass over [outer, length, inner]:
+// MODE 0 sum  (g + 0), 1 mean ((g / length) + 0), 2 max (g at the argmax
+// index, +0 elsewhere -- cpu::scatter_axis, cpu_backend.cpp:462-471).
+// The output is walked as rows: with inner == 1 a row is one outer slice of
+// `length` values sharing g[o]; with inner > 1 a row is (o, a) and holds
+// `inner` values copied from g[o, :]. One division per row, 128-bit stores.
+// ---------------------------------------------------------------------------
+template <int MODE>
+__device__ __forceinline__ float expand_value(float gv, long long w, unsigned long long a, float len) {
+    if constexpr (MODE == 0) return gv + 0.0f;
+    else if constexpr (MODE == 1) return (gv / len) + 0.0f;
+    else return static_cast<unsigned long long>(w) == a ? gv : 0.0f;
+}
+
+template <int MODE, bool VEC>
+__global__ void __launch_bounds__(kThreads)
+expand_rows_kernel(const float* __restrict__ g, const long long* __restrict__ idx, const float* __restrict__ idxf,
+                   float* __restrict__ out, unsigned long long outer, unsigned long long length,
+                   unsigned* __restrict__ err) {
+    const float len = static_cast<float>(length);
+    for (unsigned long long o = blockIdx.x; o < outer; o += gridDim.x) {
+        const float gv = __ldg(g + o);
+        long long w = -1;
+        if constexpr (MODE == 2) {
+            w = idx ? __ldg(idx + o) : static_cast<long long>(__ldg(idxf + o));
+            if (threadIdx.x == 0 && (w < 0 || static_cast<unsigned long long>(w) >= length)) atomicOr(err, kErrBadIndex);
+        }
+        float* row = out + o * length;
+        if constexpr (VEC) {
+            for (unsigned long long a = threadIdx.x * 4ull; a < length; a += kThreads * 4ull)
+                st4_stream(row + a, make_float4(expand_value<MODE>(gv, w, a, len), expand_value<MODE>(gv, w, a + 1, len),
+                                                expand_value<MODE>(gv, w, a + 2, len), expand_value<MODE>(gv, w, a + 3, len)));
+        } else {
+            for (unsigned long long a = threadIdx.x; a < length; a += kThreads) row[a] = expand_value<MODE>(gv, w, a, len);
+        }
+    }
+}
+
+template <int MODE, bool VEC>
+__global__ void __launch_bounds__(kThreads)
+expand_cols_kernel(const float* __restrict__ g, const long long* __restrict__ idx, const float* __restrict__ idxf,
+                   float* __restrict__ out, unsigned long long outer, unsigned long long length,
+                   unsigned long long inner, unsigned* __restrict__ err) {
+    const float len = static_cast<float>(length);
+    const unsigned long long rows = outer * length;
+    for (unsigned long long t = blockIdx.x; t < rows; t += gridDim.x) {
+        const unsigned long long o = t / length, a = t - o * length;
+        const float* grow = g + o * inner;
+        float* orow = out + t * inner;
+        if constexpr (VEC) {
+            for (unsigned long long i = threadIdx.x * 4ull; i < inner; i += kThreads * 4ull) {
+                const float4 gv = ldg4(grow + i);
+                long long w[4] = {-1, -1, -1, -1};
+                if constexpr (MODE == 2) {
+                    for (int u = 0; u < 4; ++u) {
+                        const unsigned long long k = o * inner + i + u;
+                        w[u] = idx ? __ldg(idx + k) : static_cast<long long>(__ldg(idxf + k));
+                        if (a == 0 && (w[u] < 0 || static_cast<unsigned long long>(w[u]) >= length)) atomicOr(err, kErrBadIndex);
+                    }
+                }
+                st4_stream(orow + i, make_float4(expand_value<MODE>(gv.x, w[0], a, len), expand_value<MODE>(gv.y, w[1], a, len),
+                                                 expand_value<MODE>(gv.z, w[2], a, len), expand_value<MODE>(gv.w, w[3], a, len)));
+            }
+        } else {
+            for (unsigned long long i = threadIdx.x; i < inner; i += kThreads) {
+                const unsigned long long k = o * inner + i;
+                long long w = -1;
+                if constexpr (MODE == 2) {
+                    w = idx ? __ldg(idx + k) : static_cast<long long>(__ldg(idxf + k));
+                    if (a == 0 && (w < 0 || static_cast<unsigned long long>(w) >= length)) atomicOr(err, kErrBadIndex);
+                }
+                orow[i] = expand_value<MODE>(__ldg(grow + i), w, a, len);
+            }
+        }
+    }
+}
+
+template <int MODE>
+static void launch_expand_mode(const float* g, const long long* idx, const float* idxf, float* out,
+                               std::size_t outer, std::size_t length, std::size_t inner) {
+    cudaStream_t st = stream();
+    unsigned* err = device_error_word();
+    if (inner == 1) {
+        const bool vec = length % 4 == 0 && aligned16(out);
+        const unsigned grid = static_cast<unsigned>(std::min<std::size_t>(outer, static_cast<std::size_t>(sm_count()) * 16));
+        if (vec) expand_rows_kernel<MODE, true><<<grid, kThreads, 0, st>>>(g, idx, idxf, out, outer, length, err);
+        else expand_rows_kernel<MODE, false><<<grid, kThreads, 0, st>>>(g, idx, idxf, out, outer, length, err);
+    } else {
+        const bool vec = inner % 4 == 0 && aligned16(out) && aligned16(g);
+        const unsigned grid = static_cast<unsigned>(std::min<std::size_t>(outer * length, static_cast<std::size_t>(sm_count()) * 16));
+        if (vec) expand_cols_kernel<MODE, true><<<grid, kThreads, 0, st>>>(g, idx, idxf, out, outer, length, inner, err);
+        else expand_cols_kernel<MODE, false><<<grid, kThreads, 0, st>>>(g, idx, idxf, out, outer, length, inner, err);
+    }
+    check_launch("axis_expand");
+}
+
+static void launch_axis_expand(int mode, const float* g, const long long* idx, const float* idxf, float* out,
+                               std::size_t outer, std::size_t length, std::size_t inner) {
+    if (!outer || !length || !inner) return;
+    if (!g || !out) fail(VC_ERR_INVALID, "axis backward: null pointer");
+    if (mode == 0) launch_expand_mode<0>(g, idx, idxf, out, outer, length, inner);
+    else if (mode == 1) launch_expand_mode<1>(g, idx, idxf, out, outer, length, inner);
+    else launch_expand_mode<2>(g, idx, idxf, out, outer, length, inner);
+}
+
+}  // namespace
+
+}  // namespace vc
+
+using namespace vc;
+
+extern "C" {
+
+vc_status vc_cuda_sum_to_shape(const float* g, const size_t* g_shape, int g_rank, float* out,
+                               const size_t* t_shape, int t_rank) {
+    VC_API_BEGIN
+    ensure_init();
+    validate_rank(g_rank, "sum_to_shape");
+    validate_rank(t_rank, "sum_to_shape");
+    if (checked_numel(t_shape, t_rank) == 0) return VC_OK;
+    if (!g || !out) fail(VC_ERR_INVALID, "sum_to_shape: null pointer");
+    Src ops[3];
+    ops[0] = align(g, g_shape, g_rank, g_shape, g_rank, "sum_to_shape");
+    if (checked_numel(g_shape, g_rank) == 0) {
+        VC_CUDA(cudaMemsetAsync(out, 0, checked_numel(t_shape, t_rank) * sizeof(float), stream()));
+        return VC_OK;
+    }
+    vjp_reduce(V_G, ops, g_shape, g_rank, t_shape, t_rank, out);
+    VC_API_END
+}
+
+vc_status vc_cuda_binary_backward(int op, const float* a, const size_t* a_shape, int a_rank,
+                                  const float* b, const size_t* b_shape, int b_rank,
+                                  const float* g, const size_t* g_shape, int g_rank,
+                                  float* da, float* db) {
+    VC_API_BEGIN
+    ensure_init();
+    validate_rank(a_rank, "binary_backward");
+    validate_rank(b_rank, "binary_backward");
+    validate_rank(g_rank, "binary_backward");
+    if (op < VC_ADD || op > VC_DIV) fail(VC_ERR_INVALID, "unknown binary operation");
+    // Output (source) shape = broadcast(a, b).
+    const int rank = std::max(a_rank, b_rank);
+    size_t src[kMaxRank];
+    for (int i = 0; i < rank; ++i) {
+        const size_t ad = i < rank - a_rank ? 1 : a_shape[i - (rank - a_rank)];
+        const size_t bd = i < rank - b_rank ? 1 : b_shape[i - (rank - b_rank)];
+        if (ad != bd && ad != 1 && bd != 1) fail(VC_ERR_INVALID, "binary_backward: operand shapes do not broadcast");
+        src[i] = std::max(ad, bd);
+    }
+    const std::size_t n = checked_numel(src, rank);
+    if (!g) fail(VC_ERR_INVALID, "binary_backward: null gradient");
+    if (n == 0) {
+        if (da) VC_CUDA(cudaMemsetAsync(da, 0, checked_numel(a_shape, a_rank) * sizeof(float), stream()));
+        if (db) VC_CUDA(cudaMemsetAsync(db, 0, checked_numel(b_shape, b_rank) * sizeof(float), stream()));
+        return VC_OK;
+    }
+    const Src sg = align(g, g_shape, g_rank, src, rank, "binary_backward");
+    const Src sa = align(a, a_shape, a_rank, src, rank, "binary_backward");
+    const Src sb = align(b, b_shape, b_rank, src, rank, "binary_backward");
+    auto same = [&](const size_t* s, int r) {
+        if (r != rank) return false;
+        for (int i = 0; i < r; ++i) if (s[i] != src[i]) return false;
+        return true;
+    };
+    if (da && db && same(a_shape, a_rank) && same(b_shape, b_rank) && same(g_shape, g_rank)) {
+        const bool vec = aligned16(a) && aligned16(b) && aligned16(g) && aligned16(da) && aligned16(db);
+        const unsigned grid = grid_for(vec ? (n + 3) / 4 : n, kThreads);
+#define VC_BB(OP) do { if (vec) binary_backward_flat<OP, true><<<grid, kThreads, 0, stream()>>>(a, b, g, da, db, n); \
+                       else binary_backward_flat<OP, false><<<grid, kThreads, 0, stream()>>>(a, b, g, da, db, n); } while (0)
+        switch (op) {
+            case VC_ADD: VC_BB(VC_ADD); break;
+            case VC_SUB: VC_BB(VC_SUB); break;
+            case VC_MUL: VC_BB(VC_MUL); break;
+            default: VC_BB(VC_DIV); break;
+        }
+#undef VC_BB
+        check_launch("binary_backward_flat");
+        return VC_OK;
+    }
+    if (da) {
+        Src ops[3] = {sg, sb, sb};
+        const int f = (op == VC_ADD || op == VC_SUB) ? V_G : (op == VC_MUL ? V_MUL : V_DIV_A);
+        vjp_reduce(f, ops, src, rank, a_shape, a_rank, da);
+    }
+    if (db) {
+        Src ops[3] = {sg, sa, sb};
+        const int f = op == VC_ADD ? V_G : (op == VC_SUB ? V_NEG : (op == VC_MUL ? V_MUL : V_DIV_B));
+        vjp_reduce(f, ops, src, rank, b_shape, b_rank, db);
+    }
+    VC_API_END
+}
+
+vc_status vc_cuda_reduce_all(int op, const float* in, size_t count, float* out_value, int64_t* out_index) {
+    VC_API_BEGIN
+    ensure_init();
+    if (!in && count) fail(VC_ERR_INVALID, "reduce_all: null input");
+    if (op == VC_REDUCE_SUM || op == VC_REDUCE_MEAN) {
+        if (!out_value) fail(VC_ERR_INVALID, "reduce_all: null output");
+        if (count == 0) {
+            if (op == VC_REDUCE_MEAN) fail(VC_ERR_INVALID, "mean of an empty tensor is undefined");
+            VC_CUDA(cudaMemsetAsync(out_value, 0, sizeof(float), stream()));
+            return VC_OK;
+        }
+        Src ops[3];
+        const size_t shape[1] = {count};
+        ops[0] = align(in, shape, 1, shape, 1, "reduce_all");
+        vjp_reduce(V_G, ops, shape, 1, nullptr, 0, out_value,
+                   op == VC_REDUCE_MEAN ? static_cast<float>(count) : 0.0f);
+        return VC_OK;
+    }
+    if (op != VC_REDUCE_MAX && op != VC_REDUCE_ARGMAX) fail(VC_ERR_INVALID, "unknown reduction");
+    if (count == 0) fail(VC_ERR_INVALID, "max of an empty tensor is undefined");
+    MaxOut o{out_value, reinterpret_cast<long long*>(out_index), op == VC_REDUCE_ARGMAX, 0, 0};
+    launch_max(in, 1, count, 1, o);
+    VC_API_END
+}
+
+vc_status vc_cuda_reduce_axis(int op, const float* in, size_t outer, size_t length, size_t inner,
+                              float* out_value, int64_t* out_index) {
+    VC_API_BEGIN
+    ensure_init();
+    const size_t dims[3] = {outer, length, inner};
+    checked_numel(dims, 3);
+    if (op == VC_REDUCE_SUM || op == VC_REDUCE_MEAN) {
+        if (op == VC_REDUCE_MEAN && length == 0) fail(VC_ERR_INVALID, "mean over an empty axis is undefined");
+        if (outer * inner == 0) return VC_OK;
+        if (!out_value) fail(VC_ERR_INVALID, "reduce_axis: null output");
+        if (length == 0) {
+            VC_CUDA(cudaMemsetAsync(out_value, 0, outer * inner * sizeof(float), stream()));
+            return VC_OK;
+        }
+        Src ops[3];
+        const size_t target[3] = {outer, 1, inner};
+        ops[0] = align(in, dims, 3, dims, 3, "reduce_axis");
+        vjp_reduce(V_G, ops, dims, 3, target, 3, out_value,
+                   op == VC_REDUCE_MEAN ? static_cast<float>(length) : 0.0f);
+        return VC_OK;
+    }
+    if (op != VC_REDUCE_MAX && op != VC_REDUCE_ARGMAX) fail(VC_ERR_INVALID, "unknown reduction");
+    if (length == 0) fail(VC_ERR_INVALID, "max/argmax over an empty axis is undefined");
+    MaxOut o{out_value, reinterpret_cast<long long*>(out_index), op == VC_REDUCE_ARGMAX, 0, 0};
+    launch_max(in, outer, length, inner, o);
+    VC_API_END
+}
+
+vc_status vc_cuda_scatter_axis(const float* values, const float* indices_f32, const int64_t* indices_i64,
+                               float* out, size_t outer, size_t length, size_t inner) {
+    VC_API_BEGIN
+    ensure_init();
+    if ((indices_f32 == nullptr) == (indices_i64 == nullptr))
+        fail(VC_ERR_INVALID, "scatter_axis: pass exactly one of the float or int64 indices");
+    launch_axis_expand(2, values, reinterpret_cast<const long long*>(indices_i64), indices_f32, out, outer, length, inner);
+    VC_API_END
+}
+
+vc_status vc_cuda_reduce_axis_backward(int op, const float* g, const int64_t* indices, float* out,
+                                       size_t outer, size_t length, size_t inner) {
+    VC_API_BEGIN
+    ensure_init();
+    int mode;
+    switch (op) {
+        case VC_REDUCE_SUM: mode = 0; break;
+        case VC_REDUCE_MEAN: mode = 1; break;
+        case VC_REDUCE_MAX:
+            if (!indices) fail(VC_ERR_INVALID, "reduce_axis_backward: max needs the argmax indices");
+            mode = 2;
+            break;
+        default: fail(VC_ERR_INVALID, "reduce_axis_backward: operation has no backward rule");
+    }
+    launch_axis_expand(mode, g, reinterpret_cast<const long long*>(indices), nullptr, out, outer, length, inner);
+    VC_API_END
+}
+
+}  // extern "C"

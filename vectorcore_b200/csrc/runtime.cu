@@ -1,0 +1,407 @@
+// runtime.cu -- device selection, the enqueue stream, the stream-ordered
+// size-class buffer pool, error reporting and the memory entry points.
+//
+// Design (B200-first, mirroring what the Metal host does in
+// src/metal/metal_backend.mm):
+//  * one process drives one GPU; all work goes to one CUDA stream, so work
+//    executes in submission order (Metal: one serial command queue, :517-560);
+//  * buffers come from a size-class pool (256 B minimum, powers of two up to
+//    4 MiB, then 1 MiB steps -- the same classes as bucket_bytes, :487-499).
+//    A freed block is reusable immediately: its next user is enqueued after
+//    every earlier user on the same stream, which is the ordering Metal needs a
+//    completion handler for (:184-191, :531-554);
+//  * the pool keeps at most VC_CUDA_POOL_LIMIT bytes cached (default 96 GiB,
+//    sized for 180 GB of HBM3e); on cudaMalloc failure it returns every cached
+//    block to the driver and retries once;
+//  * kernels that detect a problem set bits in a device error word; blocking
+//    calls read and clear it and report the failure (Metal: async_error_,
+//    :428-443).
+#include "vc_internal.cuh"
+
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <unordered_map>
+#include <vector>
+
+namespace vc {
+
+namespace {
+
+thread_local std::string t_last_error;
+
+struct Pool {
+    std::mutex mutex;
+    std::map<std::size_t, std::vector<void*>> free_blocks;  // bucket bytes -> blocks
+    std::unordered_map<void*, std::size_t> live;             // block -> bucket bytes
+    std::size_t cached_bytes{0};
+    std::size_t in_use_bytes{0};
+    std::size_t hits{0};
+    std::size_t misses{0};
+    std::size_t limit{96ull << 30};
+};
+
+struct State {
+    std::mutex init_mutex;
+    bool ready{false};
+    int device{-1};
+    int sms{148};
+    cudaStream_t own_stream{nullptr};
+    cudaStream_t stream{nullptr};
+    unsigned* counters{nullptr};
+    unsigned* error_word{nullptr};
+    char name[256]{};
+    Pool pool;
+};
+
+State& state() {
+    static State* s = new State();  // never destroyed: tensors may outlive static teardown
+    return *s;
+}
+
+std::size_t bucket_bytes(std::size_t bytes) {
+    constexpr std::size_t kMin = 256, kPow2Limit = 4u << 20, kStep = 1u << 20;
+    if (bytes <= kMin) return kMin;
+    if (bytes <= kPow2Limit) {
+        std::size_t b = kMin;
+        while (b < bytes) b <<= 1;
+        return b;
+    }
+    return (bytes + kStep - 1) / kStep * kStep;
+}
+
+void release_cached_locked(Pool& pool) {
+    for (auto& entry : pool.free_blocks)
+        for (void* p : entry.second) cudaFree(p);
+    pool.free_blocks.clear();
+    pool.cached_bytes = 0;
+}
+
+}  // namespace
+
+void set_last_error(const std::string& message) { t_last_error = message; }
+
+void fail(vc_status status, const std::string& message) { throw Error(status, message); }
+
+void check_cuda(cudaError_t err, const char* what) {
+    if (err == cudaSuccess) return;
+    const vc_status st = err == cudaErrorMemoryAllocation ? VC_ERR_OOM : VC_ERR_RUNTIME;
+    throw Error(st, std::string("CUDA error in ") + what + ": " + cudaGetErrorString(err));
+}
+
+void check_launch(const char* what) {
+    const cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess)
+        throw Error(VC_ERR_RUNTIME, std::string("kernel launch failed (") + what + "): " +
+                                        cudaGetErrorString(err));
+}
+
+static void init_device(int device) {
+    State& s = state();
+    std::lock_guard<std::mutex> lock(s.init_mutex);
+    if (s.ready) {
+        if (device == s.device) return;
+        fail(VC_ERR_INVALID, "the VectorCore CUDA device is already bound to GPU " +
+                                 std::to_string(s.device) + " in this process");
+    }
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+        cudaGetLastError();
+        fail(VC_ERR_RUNTIME, "no CUDA device is available");
+    }
+    if (device < 0 || device >= count) fail(VC_ERR_OUT_OF_RANGE, "CUDA device index out of range");
+    cudaDeviceProp prop{};
+    VC_CUDA(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10)
+        fail(VC_ERR_RUNTIME, std::string("the VectorCore CUDA device is built for sm_100a (B200); "
+                                         "found ") + prop.name);
+    VC_CUDA(cudaSetDevice(device));
+    VC_CUDA(cudaStreamCreateWithFlags(&s.own_stream, cudaStreamNonBlocking));
+    s.stream = s.own_stream;
+    s.sms = prop.multiProcessorCount;
+    std::snprintf(s.name, sizeof s.name, "%s", prop.name);
+    VC_CUDA(cudaMalloc(&s.counters, kCounterSlots * sizeof(unsigned)));
+    VC_CUDA(cudaMemset(s.counters, 0, kCounterSlots * sizeof(unsigned)));
+    VC_CUDA(cudaMalloc(&s.error_word, sizeof(unsigned)));
+    VC_CUDA(cudaMemset(s.error_word, 0, sizeof(unsigned)));
+    if (const char* lim = std::getenv("VC_CUDA_POOL_LIMIT")) s.pool.limit = std::strtoull(lim, nullptr, 10);
+    s.device = device;
+    s.ready = true;
+}
+
+void ensure_init() {
+    if (!state().ready) init_device(0);
+    // Work may be issued from any host thread: make sure it targets our GPU.
+    int current = -1;
+    if (cudaGetDevice(&current) == cudaSuccess && current != state().device) VC_CUDA(cudaSetDevice(state().device));
+}
+
+cudaStream_t stream() { return state().stream; }
+int sm_count() { return state().sms; }
+unsigned* counters() { return state().counters; }
+unsigned* device_error_word() { return state().error_word; }
+
+static void* pool_alloc(std::size_t bytes) {
+    ensure_init();
+    State& s = state();
+    Pool& pool = s.pool;
+    const std::size_t b = bucket_bytes(bytes ? bytes : 1);
+    {
+        std::lock_guard<std::mutex> lock(pool.mutex);
+        auto it = pool.free_blocks.find(b);
+        if (it != pool.free_blocks.end() && !it->second.empty()) {
+            void* p = it->second.back();
+            it->second.pop_back();
+            pool.cached_bytes -= b;
+            pool.in_use_bytes += b;
+            pool.live[p] = b;
+            ++pool.hits;
+            return p;
+        }
+        ++pool.misses;
+    }
+    if (std::getenv("VC_CUDA_FAKE_OOM")) fail(VC_ERR_OOM, "device allocation failed (VC_CUDA_FAKE_OOM)");
+    void* p = nullptr;
+    cudaError_t err = cudaMalloc(&p, b);
+    if (err == cudaErrorMemoryAllocation) {
+        cudaGetLastError();
+        // Cached blocks may still be referenced by enqueued work: finish it,
+        // hand the cache back to the driver and retry once.
+        VC_CUDA(cudaStreamSynchronize(s.stream));
+        {
+            std::lock_guard<std::mutex> lock(pool.mutex);
+            release_cached_locked(pool);
+        }
+        err = cudaMalloc(&p, b);
+    }
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        fail(VC_ERR_OOM, "device allocation of " + std::to_string(b) + " bytes failed: " +
+                             cudaGetErrorString(err));
+    }
+    std::lock_guard<std::mutex> lock(pool.mutex);
+    pool.in_use_bytes += b;
+    pool.live[p] = b;
+    return p;
+}
+
+static void pool_free(void* p) {
+    if (!p) return;
+    State& s = state();
+    Pool& pool = s.pool;
+    std::lock_guard<std::mutex> lock(pool.mutex);
+    auto it = pool.live.find(p);
+    if (it == pool.live.end()) fail(VC_ERR_INVALID, "vc_cuda_free: pointer was not allocated by the pool");
+    const std::size_t b = it->second;
+    pool.live.erase(it);
+    pool.in_use_bytes -= b;
+    if (pool.cached_bytes + b > pool.limit) {
+        // Over the cache limit: let the driver have it (cudaFree waits for
+        // the device, so enqueued users finish first).
+        cudaFree(p);
+        return;
+    }
+    pool.free_blocks[b].push_back(p);
+    pool.cached_bytes += b;
+}
+
+Scratch::Scratch(std::size_t bytes) : ptr_(pool_alloc(bytes)) {}
+Scratch::~Scratch() {
+    try {
+        pool_free(ptr_);
+    } catch (...) {
+    }
+}
+
+std::size_t checked_numel(const size_t* shape, int rank) {
+    std::size_t total = 1;
+    for (int i = 0; i < rank; ++i) {
+        const std::size_t d = shape[i];
+        if (d != 0 && total > SIZE_MAX / d) fail(VC_ERR_OVERFLOW, "tensor element count overflows size_t");
+        total *= d;
+    }
+    return total;
+}
+
+void validate_rank(int rank, const char* what) {
+    if (rank < 0 || rank > kMaxRank)
+        fail(VC_ERR_INVALID, std::string(what) + ": the CUDA device supports tensors of rank 0.." +
+                                 std::to_string(kMaxRank));
+}
+
+static void surface_device_errors() {
+    State& s = state();
+    unsigned word = 0;
+    VC_CUDA(cudaMemcpy(&word, s.error_word, sizeof word, cudaMemcpyDeviceToHost));
+    if (!word) return;
+    VC_CUDA(cudaMemset(s.error_word, 0, sizeof(unsigned)));
+    std::string what;
+    if (word & kErrBadTarget) what += "cross_entropy target class out of range; ";
+    if (word & kErrBadIndex) what += "scatter index out of range; ";
+    if (word & kErrWaitTimeout) what += "a bounded device-side wait timed out; ";
+    fail(word & kErrWaitTimeout ? VC_ERR_TIMEOUT : VC_ERR_OUT_OF_RANGE,
+         "CUDA device reported: " + what.substr(0, what.size() - 2));
+}
+
+}  // namespace vc
+
+using namespace vc;
+
+extern "C" {
+
+int vc_cuda_available(void) {
+    try {
+        ensure_init();
+        return 1;
+    } catch (const Error& e) {
+        set_last_error(e.what());
+        return 0;
+    }
+}
+
+vc_status vc_cuda_init(int device) {
+    VC_API_BEGIN
+    init_device(device);
+    VC_API_END
+}
+
+const char* vc_cuda_last_error(void) { return t_last_error.c_str(); }
+
+vc_status vc_cuda_device_name(char* buffer, size_t length) {
+    VC_API_BEGIN
+    ensure_init();
+    if (!buffer || !length) fail(VC_ERR_INVALID, "vc_cuda_device_name: empty buffer");
+    std::snprintf(buffer, length, "%s", state().name);
+    VC_API_END
+}
+
+vc_status vc_cuda_synchronize(void) {
+    VC_API_BEGIN
+    ensure_init();
+    VC_CUDA(cudaStreamSynchronize(state().stream));
+    surface_device_errors();
+    VC_API_END
+}
+
+void* vc_cuda_stream(void) {
+    try {
+        ensure_init();
+        return state().stream;
+    } catch (const Error& e) {
+        set_last_error(e.what());
+        return nullptr;
+    }
+}
+
+vc_status vc_cuda_set_stream(void* s) {
+    VC_API_BEGIN
+    ensure_init();
+    State& st = state();
+    cudaStream_t next = s ? static_cast<cudaStream_t>(s) : st.own_stream;
+    if (next == st.stream) return VC_OK;
+    // Pooled blocks were last used on the old stream: drain it so their
+    // reuse on the new one is ordered.
+    VC_CUDA(cudaStreamSynchronize(st.stream));
+    st.stream = next;
+    VC_API_END
+}
+
+int vc_cuda_sm_count(void) {
+    try {
+        ensure_init();
+        return state().sms;
+    } catch (const Error& e) {
+        set_last_error(e.what());
+        return 0;
+    }
+}
+
+vc_status vc_cuda_alloc(size_t bytes, void** pointer) {
+    VC_API_BEGIN
+    if (!pointer) fail(VC_ERR_INVALID, "vc_cuda_alloc: null output pointer");
+    *pointer = pool_alloc(bytes);
+    VC_API_END
+}
+
+vc_status vc_cuda_free(void* pointer) {
+    VC_API_BEGIN
+    if (!state().ready) return VC_OK;
+    pool_free(pointer);
+    VC_API_END
+}
+
+vc_status vc_cuda_pool_stats(size_t* cached_bytes, size_t* in_use_bytes, size_t* hits,
+                             size_t* misses) {
+    VC_API_BEGIN
+    Pool& pool = state().pool;
+    std::lock_guard<std::mutex> lock(pool.mutex);
+    if (cached_bytes) *cached_bytes = pool.cached_bytes;
+    if (in_use_bytes) *in_use_bytes = pool.in_use_bytes;
+    if (hits) *hits = pool.hits;
+    if (misses) *misses = pool.misses;
+    VC_API_END
+}
+
+vc_status vc_cuda_pool_trim(void) {
+    VC_API_BEGIN
+    ensure_init();
+    VC_CUDA(cudaStreamSynchronize(state().stream));
+    Pool& pool = state().pool;
+    std::lock_guard<std::mutex> lock(pool.mutex);
+    release_cached_locked(pool);
+    VC_API_END
+}
+
+vc_status vc_cuda_host_alloc(size_t bytes, void** pointer) {
+    VC_API_BEGIN
+    ensure_init();
+    if (!pointer) fail(VC_ERR_INVALID, "vc_cuda_host_alloc: null output pointer");
+    VC_CUDA(cudaHostAlloc(pointer, bytes ? bytes : 1, cudaHostAllocPortable));
+    VC_API_END
+}
+
+vc_status vc_cuda_host_free(void* pointer) {
+    VC_API_BEGIN
+    if (pointer) VC_CUDA(cudaFreeHost(pointer));
+    VC_API_END
+}
+
+vc_status vc_cuda_upload(void* dst, const void* src, size_t bytes) {
+    VC_API_BEGIN
+    ensure_init();
+    if (!bytes) return VC_OK;
+    if (!dst || !src) fail(VC_ERR_INVALID, "vc_cuda_upload: null pointer");
+    cudaPointerAttributes attr{};
+    const bool pinned = cudaPointerGetAttributes(&attr, src) == cudaSuccess &&
+                        attr.type == cudaMemoryTypeHost;
+    cudaGetLastError();
+    VC_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, state().stream));
+    // Pageable sources are staged by the driver before cudaMemcpyAsync
+    // returns; a pinned source is read later, so wait for this copy to keep
+    // the "src may be reused on return" contract.
+    if (pinned) VC_CUDA(cudaStreamSynchronize(state().stream));
+    VC_API_END
+}
+
+vc_status vc_cuda_download(void* dst, const void* src, size_t bytes) {
+    VC_API_BEGIN
+    ensure_init();
+    if (!bytes) return VC_OK;
+    if (!dst || !src) fail(VC_ERR_INVALID, "vc_cuda_download: null pointer");
+    VC_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, state().stream));
+    VC_CUDA(cudaStreamSynchronize(state().stream));
+    surface_device_errors();
+    VC_API_END
+}
+
+vc_status vc_cuda_copy(void* dst, const void* src, size_t bytes) {
+    VC_API_BEGIN
+    ensure_init();
+    if (!bytes) return VC_OK;
+    VC_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, state().stream));
+    VC_API_END
+}
+
+}  // extern "C"

@@ -1,0 +1,532 @@
+// softmax.cu -- fused softmax, log_softmax and softmax cross-entropy
+// (forward and backward) for sm_100a.
+//
+// The reference composes these from primitive ops -- six launches and four
+// full-size temporaries for log_softmax, plus a host-built one-hot mask for
+// cross-entropy (src/ops.cpp:378-388, src/nn.cpp:31-53). Here each is ONE
+// pass over HBM: read x (and g) once, write the result once.
+//
+// Rows (reduction over the last axis): one thread-block cluster of C CTAs per
+// row, C in {1, 2, 4, 8} chosen so a CTA's slice of the row is at most 8K
+// floats (32 KB) -- small enough for several CTAs per SM so one CTA's loads
+// overlap another's arithmetic. Each CTA stages its slice in shared memory
+// with one TMA bulk copy (cp.async.bulk, completion on an mbarrier; no
+// multicast), reduces it, and the C partials are exchanged through
+// distributed shared memory and combined in rank order, so every CTA of the
+// cluster derives the same row statistics. Other axes (and rows too long for
+// a cluster) take a column kernel that walks the axis in global memory.
+//
+// The arithmetic is the reference's, operation by operation:
+//   m  = max(x) with the scan semantics of cpu::reduce_axis,
+//   s  = float(double sum of expf(x - m)),  l = logf(s),
+//   log_softmax = (x - m) - l,  softmax = expf(log_softmax),
+// and the backward passes replay the reference autograd chain (engine order
+// of src/tensor.cpp:266-300) from the saved m and s:
+//   log_softmax: dx = g + ((float(sum(-g)) / s) + 0) * expf(x - m)
+//   softmax:     gy = g * y;  dx = gy + ((float(sum(-gy)) / s) + 0) * expf(x - m)
+//   cross-entropy (upstream u, batch B): dp = (-(u / B)) + 0,
+//     dx = dp * onehot + ((dl / s) + 0) * expf(x - m) with dl = sum(-dp*onehot).
+// Results therefore differ from the CPU path only through expf/logf ulps and
+// the order of double additions.
+#include "vc_internal.cuh"
+
+#include <cooperative_groups.h>
+
+#include <algorithm>
+#include <cmath>
+
+namespace cg = cooperative_groups;
+
+namespace vc {
+
+namespace {
+
+constexpr unsigned kThreads = 256;
+constexpr unsigned kSliceTarget = 8192;     // floats per CTA slice (32 KB)
+constexpr unsigned kSliceMax = 24576;       // floats per CTA slice at cluster size 8 (96 KB)
+constexpr long long kWaitSpins = 1ll << 24; // bounded mbarrier wait (iterations)
+
+enum Mode { LSM_FWD = 0, SM_FWD = 1, CE_FWD = 2, LSM_BWD = 3, SM_BWD = 4 };
+
+// ---- TMA bulk copy + mbarrier helpers --------------------------------------
+__device__ __forceinline__ unsigned smem_addr(const void* p) {
+    return static_cast<unsigned>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(unsigned long long* bar, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(unsigned long long* bar, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, unsigned bytes, unsigned long long* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned parity) {
+    unsigned ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Wait for phase `parity` with an iteration limit; false (and the device
+// error bit) when it gave up.
+__device__ __forceinline__ bool mbar_wait_bounded(unsigned long long* bar, unsigned parity, unsigned* err) {
+    for (long long i = 0; i < kWaitSpins; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    atomicOr(err, kErrWaitTimeout);
+    return false;
+}
+
+struct RowArgs {
+    const float* x;
+    const float* g;
+    float* y;
+    float* row_max;    // in (bwd) or out (fwd), per row
+    float* row_sum;
+    const long long* targets;
+    float* row_term;   // CE: per-row log_softmax at the target
+    unsigned long long rows;
+    unsigned long long L;
+    unsigned seg;      // floats per CTA slice (multiple of 4)
+    unsigned* err;
+};
+
+__device__ __forceinline__ MaxCand cluster_max(cg::cluster_group& cluster, MaxCand mine, float* s_v, long long* s_i,
+                                               unsigned C) {
+    if (threadIdx.x == 0) { *s_v = mine.v; *s_i = mine.i; }
+    cluster.sync();
+    MaxCand c{0.0f, -1};
+    for (unsigned r = 0; r < C; ++r) {
+        const float v = *cluster.map_shared_rank(s_v, r);
+        const long long i = *cluster.map_shared_rank(s_i, r);
+        c = max_combine(c, MaxCand{v, i});
+    }
+    return c;
+}
+
+__device__ __forceinline__ double cluster_sum(cg::cluster_group& cluster, double mine, double* s_d, unsigned C) {
+    if (threadIdx.x == 0) *s_d = mine;
+    cluster.sync();
+    double t = 0.0;
+    for (unsigned r = 0; r < C; ++r) t += *cluster.map_shared_rank(s_d, r);
+    return t;
+}
+
+// One cluster per row. Dynamic shared memory: [slice of x][slice of g].
+template <int MODE, bool BULK>
+__global__ void __launch_bounds__(kThreads)
+row_kernel(const RowArgs a, unsigned long long row0) {
+    extern __shared__ __align__(128) float smem[];
+    __shared__ unsigned long long bar;
+    __shared__ double s_red[32];
+    __shared__ float s_mv[32];
+    __shared__ long long s_mi[32];
+    __shared__ float x_mv;          // cluster exchange slots (one per phase)
+    __shared__ long long x_mi;
+    __shared__ double x_sum;
+    __shared__ double x_sum2;
+
+    cg::cluster_group cluster = cg::this_cluster();
+    const unsigned C = cluster.num_blocks();
+    const unsigned rank = cluster.block_rank();
+    const unsigned long long row = row0 + blockIdx.x / C;
+    if (row >= a.rows) return;  // whole cluster exits together (same row)
+
+    constexpr bool STAGE_X = MODE == LSM_FWD || MODE == SM_FWD || MODE == CE_FWD || MODE == SM_BWD;
+    constexpr bool STAGE_G = MODE == LSM_BWD || MODE == SM_BWD;
+    const unsigned long long c0 = static_cast<unsigned long long>(rank) * a.seg;
+    const unsigned n = c0 < a.L ? static_cast<unsigned>(min(static_cast<unsigned long long>(a.seg), a.L - c0)) : 0u;
+    float* sx = smem;
+    float* sg = smem + (STAGE_X ? a.seg : 0);
+    const float* xrow = a.x + row * a.L + c0;
+    const float* grow = STAGE_G || MODE == LSM_BWD ? a.g + row * a.L + c0 : nullptr;
+
+    // ---- stage the slice(s) ------------------------------------------------
+    bool staged = true;
+    if constexpr (BULK) {
+        const unsigned bytes = n * 4u * ((STAGE_X ? 1u : 0u) + (STAGE_G ? 1u : 0u));
+        if (threadIdx.x == 0) {
+            mbar_init(&bar, 1);
+            mbar_fence_init();
+        }
+        __syncthreads();
+        if (threadIdx.x == 0 && bytes) {
+            mbar_expect_tx(&bar, bytes);
+            if (STAGE_X) bulk_load(sx, xrow, n * 4u, &bar);
+            if (STAGE_G) bulk_load(sg, grow, n * 4u, &bar);
+        }
+        if (bytes) staged = mbar_wait_bounded(&bar, 0, a.err);
+    } else {
+        for (unsigned k = threadIdx.x; k < n; k += kThreads) {
+            if (STAGE_X) sx[k] = __ldg(xrow + k);
+            if (STAGE_G) sg[k] = __ldg(grow + k);
+        }
+        __syncthreads();
+    }
+
+    float m, s;
+    if constexpr (MODE == LSM_FWD || MODE == SM_FWD || MODE == CE_FWD) {
+        // ---- row max (scan semantics) ----
+        MaxCand c{0.0f, -1};
+        for (unsigned k = threadIdx.x; k < n; k += kThreads) c = max_take(c, sx[k], static_cast<long long>(c0 + k));
+        c = block_max(c, s_mv, s_mi);
+        c = cluster_max(cluster, c, &x_mv, &x_mi, C);
+        const float first = __ldg(a.x + row * a.L);
+        m = first != first ? first : c.v;
+        // ---- row sum of expf(x - m), double ----
+        double acc = 0.0;
+        for (unsigned k = threadIdx.x; k < n; k += kThreads) acc += static_cast<double>(expf(sx[k] - m));
+        acc = block_sum(acc, s_red);
+        s = static_cast<float>(cluster_sum(cluster, acc, &x_sum, C));
+        const float l = logf(s);
+        if (rank == 0 && threadIdx.x == 0) {
+            if (a.row_max) a.row_max[row] = m;
+            if (a.row_sum) a.row_sum[row] = s;
+        }
+        if constexpr (MODE == CE_FWD) {
+            const long long t = __ldg(a.targets + row);
+            if (t < 0 || static_cast<unsigned long long>(t) >= a.L) {
+                if (rank == 0 && threadIdx.x == 0) { atomicOr(a.err, kErrBadTarget); a.row_term[row] = 0.0f; }
+            } else if (threadIdx.x == 0 && static_cast<unsigned long long>(t) >= c0 &&
+                       static_cast<unsigned long long>(t) < c0 + n) {
+                a.row_term[row] = (sx[t - c0] - m) - l;
+            }
+        } else {
+            float* yrow = a.y + row * a.L + c0;
+            for (unsigned k = threadIdx.x; k < n; k += kThreads) {
+                const float ls = (sx[k] - m) - l;
+                yrow[k] = MODE == SM_FWD ? expf(ls) : ls;
+            }
+        }
+    } else {
+        m = __ldg(a.row_max + row);
+        s = __ldg(a.row_sum + row);
+        if constexpr (MODE == LSM_BWD) {
+            double acc = 0.0;
+            for (unsigned k = threadIdx.x; k < n; k += kThreads) acc += static_cast<double>(-sg[k]);
+            acc = block_sum(acc, s_red);
+            const float dl = static_cast<float>(cluster_sum(cluster, acc, &x_sum, C));
+            const float ds = dl / s;
+            const float de = ds + 0.0f;
+            float* dxrow = a.y + row * a.L + c0;
+            for (unsigned k = threadIdx.x; k < n; k += kThreads)
+                dxrow[k] = sg[k] + de * expf(__ldg(xrow + k) - m);
+        } else {  // SM_BWD
+            const float l = logf(s);
+            double acc = 0.0;
+            for (unsigned k = threadIdx.x; k < n; k += kThreads) {
+                const float y = expf((sx[k] - m) - l);
+                const float gy = sg[k] * y;
+                sg[k] = gy;
+                acc += static_cast<double>(-gy);
+            }
+            acc = block_sum(acc, s_red);
+            const float dl = static_cast<float>(cluster_sum(cluster, acc, &x_sum2, C));
+            const float ds = dl / s;
+            const float de = ds + 0.0f;
+            float* dxrow = a.y + row * a.L + c0;
+            for (unsigned k = threadIdx.x; k < n; k += kThreads) dxrow[k] = sg[k] + de * expf(sx[k] - m);
+        }
+    }
+    (void)staged;
+    // Keep this CTA's shared memory alive until every rank has read it.
+    cluster.sync();
+}
+
+// Column kernel: one thread per (o, i) position walks the axis in global
+// memory. Handles any [outer, length, inner] (inner >= 1).
+template <int MODE>
+__global__ void __launch_bounds__(kThreads)
+col_kernel(const RowArgs a, unsigned long long outer, unsigned long long inner) {
+    const unsigned long long count = outer * inner;
+    const unsigned long long stride = static_cast<unsigned long long>(gridDim.x) * blockDim.x;
+    const unsigned long long L = a.L;
+    for (unsigned long long k = static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x; k < count;
+         k += stride) {
+        const unsigned long long ob = k / inner, i = k - ob * inner;
+        const unsigned long long base = ob * L * inner + i;
+        const float* x = a.x + base;
+        float m, s;
+        if constexpr (MODE == LSM_FWD || MODE == SM_FWD || MODE == CE_FWD) {
+            MaxCand c{0.0f, -1};
+            for (unsigned long long j = 0; j < L; ++j) c = max_take(c, x[j * inner], static_cast<long long>(j));
+            m = x[0] != x[0] ? x[0] : c.v;
+            double acc = 0.0;
+            for (unsigned long long j = 0; j < L; ++j) acc += static_cast<double>(expf(x[j * inner] - m));
+            s = static_cast<float>(acc);
+            const float l = logf(s);
+            if (a.row_max) a.row_max[k] = m;
+            if (a.row_sum) a.row_sum[k] = s;
+            if constexpr (MODE == CE_FWD) {
+                const long long t = a.targets[k];
+                if (t < 0 || static_cast<unsigned long long>(t) >= L) {
+                    atomicOr(a.err, kErrBadTarget);
+                    a.row_term[k] = 0.0f;
+                } else {
+                    a.row_term[k] = (x[t * inner] - m) - l;
+                }
+            } else {
+                for (unsigned long long j = 0; j < L; ++j) {
+                    const float ls = (x[j * inner] - m) - l;
+                    a.y[base + j * inner] = MODE == SM_FWD ? expf(ls) : ls;
+                }
+            }
+        } else {
+            m = a.row_max[k];
+            s = a.row_sum[k];
+            const float* g = a.g + base;
+            if constexpr (MODE == LSM_BWD) {
+                double acc = 0.0;
+                for (unsigned long long j = 0; j < L; ++j) acc += static_cast<double>(-g[j * inner]);
+                const float de = (static_cast<float>(acc) / s) + 0.0f;
+                for (unsigned long long j = 0; j < L; ++j)
+                    a.y[base + j * inner] = g[j * inner] + de * expf(x[j * inner] - m);
+            } else {
+                const float l = logf(s);
+                double acc = 0.0;
+                for (unsigned long long j = 0; j < L; ++j) {
+                    const float y = expf((x[j * inner] - m) - l);
+                    acc += static_cast<double>(-(g[j * inner] * y));
+                }
+                const float de = (static_cast<float>(acc) / s) + 0.0f;
+                for (unsigned long long j = 0; j < L; ++j) {
+                    const float y = expf((x[j * inner] - m) - l);
+                    const float gy = g[j * inner] * y;
+                    a.y[base + j * inner] = gy + de * expf(x[j * inner] - m);
+                }
+            }
+        }
+    }
+}
+
+// loss = (-(float)(sum of row terms, double)) / B; partial = the double sum.
+__global__ void __launch_bounds__(1024)
+ce_finish_kernel(const float* __restrict__ row_term, unsigned long long rows, float batch_total,
+                 float* __restrict__ loss, double* __restrict__ partial) {
+    __shared__ double s_red[32];
+    double acc = 0.0;
+    for (unsigned long long r = threadIdx.x; r < rows; r += blockDim.x) acc += static_cast<double>(row_term[r]);
+    acc = block_sum(acc, s_red);
+    if (threadIdx.x == 0) {
+        const float t = static_cast<float>(acc);
+        const float neg = -t;
+        if (loss) *loss = neg / batch_total;
+        if (partial) *partial = acc;
+    }
+}
+
+// Cross-entropy backward: a streaming pass, no reduction needed.
+template <bool VEC>
+__global__ void __launch_bounds__(kThreads)
+ce_backward_kernel(const float* __restrict__ x, const long long* __restrict__ targets,
+                   const float* __restrict__ row_max, const float* __restrict__ row_sum,
+                   const float* __restrict__ upstream, unsigned long long rows, unsigned long long classes,
+                   float batch_total, float* __restrict__ dx) {
+    const float u = __ldg(upstream);
+    const float dn = u / batch_total;
+    const float dt = -dn;
+    const float dp = dt + 0.0f;
+    // dl = float(sum over the row of -(dp * onehot)) accumulated from +0.0.
+    float dl;
+    if (dp == 0.0f) dl = 0.0f;
+    else if (isinf(dp) && classes > 1) dl = __int_as_float(0x7fc00000);
+    else dl = -dp;
+    for (unsigned long long row = blockIdx.x; row < rows; row += gridDim.x) {
+        const float m = __ldg(row_max + row);
+        const float s = __ldg(row_sum + row);
+        const long long t = __ldg(targets + row);
+        const float de = (dl / s) + 0.0f;
+        const float* xr = x + row * classes;
+        float* dr = dx + row * classes;
+        if constexpr (VEC) {
+            for (unsigned long long c = threadIdx.x * 4ull; c < classes; c += kThreads * 4ull) {
+                const float4 xv = ldg4(xr + c);
+                float4 o;
+                o.x = dp * (static_cast<long long>(c) == t ? 1.0f : 0.0f) + de * expf(xv.x - m);
+                o.y = dp * (static_cast<long long>(c + 1) == t ? 1.0f : 0.0f) + de * expf(xv.y - m);
+                o.z = dp * (static_cast<long long>(c + 2) == t ? 1.0f : 0.0f) + de * expf(xv.z - m);
+                o.w = dp * (static_cast<long long>(c + 3) == t ? 1.0f : 0.0f) + de * expf(xv.w - m);
+                st4_stream(dr + c, o);
+            }
+        } else {
+            for (unsigned long long c = threadIdx.x; c < classes; c += kThreads)
+                dr[c] = dp * (static_cast<long long>(c) == t ? 1.0f : 0.0f) + de * expf(__ldg(xr + c) - m);
+        }
+    }
+}
+
+template <int MODE, bool BULK>
+static void launch_rows_mode(const RowArgs& a, unsigned C, std::size_t smem) {
+    static bool configured = false;
+    if (!configured) {
+        VC_CUDA(cudaFuncSetAttribute(row_kernel<MODE, BULK>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        VC_CUDA(cudaFuncSetAttribute(row_kernel<MODE, BULK>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+        configured = true;
+    }
+    const unsigned long long max_rows_per_launch = (1ull << 31) / 8 / C;
+    for (unsigned long long row0 = 0; row0 < a.rows; row0 += max_rows_per_launch) {
+        const unsigned long long rows = std::min<unsigned long long>(a.rows - row0, max_rows_per_launch);
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(static_cast<unsigned>(rows * C), 1, 1);
+        cfg.blockDim = dim3(kThreads, 1, 1);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = stream();
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = C;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        VC_CUDA(cudaLaunchKernelEx(&cfg, row_kernel<MODE, BULK>, a, row0));
+    }
+    check_launch("softmax_rows");
+}
+
+template <int MODE>
+static void launch_family(RowArgs a, std::size_t outer, std::size_t length, std::size_t inner) {
+    constexpr bool STAGE_X = MODE == LSM_FWD || MODE == SM_FWD || MODE == CE_FWD || MODE == SM_BWD;
+    constexpr bool STAGE_G = MODE == LSM_BWD || MODE == SM_BWD;
+    a.err = device_error_word();
+    a.L = length;
+    if (inner == 1 && length <= 8ull * kSliceMax) {
+        unsigned C = 1;
+        while (C < 8 && (length + C - 1) / C > kSliceTarget) C <<= 1;
+        unsigned long long seg = (length + C - 1) / C;
+        seg = (seg + 3) / 4 * 4;
+        a.seg = static_cast<unsigned>(seg);
+        a.rows = outer;
+        const std::size_t smem = seg * sizeof(float) * ((STAGE_X ? 1 : 0) + (STAGE_G ? 1 : 0));
+        const bool bulk = length % 4 == 0 && (!STAGE_X || aligned16(a.x)) && (!STAGE_G || aligned16(a.g));
+        if (bulk) launch_rows_mode<MODE, true>(a, C, smem);
+        else launch_rows_mode<MODE, false>(a, C, smem);
+        return;
+    }
+    a.rows = outer * inner;
+    col_kernel<MODE><<<grid_for(outer * inner, kThreads), kThreads, 0, stream()>>>(a, outer, inner);
+    check_launch("softmax_cols");
+}
+
+}  // namespace
+
+}  // namespace vc
+
+using namespace vc;
+
+extern "C" {
+
+static void check_dims(size_t outer, size_t length, size_t inner) {
+    const size_t dims[3] = {outer, length, inner};
+    checked_numel(dims, 3);
+}
+
+vc_status vc_cuda_log_softmax(const float* x, float* y, float* row_max, float* row_sum, size_t outer,
+                              size_t length, size_t inner) {
+    VC_API_BEGIN
+    ensure_init();
+    check_dims(outer, length, inner);
+    if (!outer || !length || !inner) return VC_OK;
+    if (!x || !y) fail(VC_ERR_INVALID, "log_softmax: null pointer");
+    RowArgs a{};
+    a.x = x; a.y = y; a.row_max = row_max; a.row_sum = row_sum;
+    launch_family<LSM_FWD>(a, outer, length, inner);
+    VC_API_END
+}
+
+vc_status vc_cuda_softmax(const float* x, float* y, float* row_max, float* row_sum, size_t outer,
+                          size_t length, size_t inner) {
+    VC_API_BEGIN
+    ensure_init();
+    check_dims(outer, length, inner);
+    if (!outer || !length || !inner) return VC_OK;
+    if (!x || !y) fail(VC_ERR_INVALID, "softmax: null pointer");
+    RowArgs a{};
+    a.x = x; a.y = y; a.row_max = row_max; a.row_sum = row_sum;
+    launch_family<SM_FWD>(a, outer, length, inner);
+    VC_API_END
+}
+
+vc_status vc_cuda_log_softmax_backward(const float* x, const float* row_max, const float* row_sum,
+                                       const float* g, float* dx, size_t outer, size_t length, size_t inner) {
+    VC_API_BEGIN
+    ensure_init();
+    check_dims(outer, length, inner);
+    if (!outer || !length || !inner) return VC_OK;
+    if (!x || !row_max || !row_sum || !g || !dx) fail(VC_ERR_INVALID, "log_softmax_backward: null pointer");
+    RowArgs a{};
+    a.x = x; a.g = g; a.y = dx;
+    a.row_max = const_cast<float*>(row_max); a.row_sum = const_cast<float*>(row_sum);
+    launch_family<LSM_BWD>(a, outer, length, inner);
+    VC_API_END
+}
+
+vc_status vc_cuda_softmax_backward(const float* x, const float* row_max, const float* row_sum,
+                                   const float* g, float* dx, size_t outer, size_t length, size_t inner) {
+    VC_API_BEGIN
+    ensure_init();
+    check_dims(outer, length, inner);
+    if (!outer || !length || !inner) return VC_OK;
+    if (!x || !row_max || !row_sum || !g || !dx) fail(VC_ERR_INVALID, "softmax_backward: null pointer");
+    RowArgs a{};
+    a.x = x; a.g = g; a.y = dx;
+    a.row_max = const_cast<float*>(row_max); a.row_sum = const_cast<float*>(row_sum);
+    launch_family<SM_BWD>(a, outer, length, inner);
+    VC_API_END
+}
+
+vc_status vc_cuda_cross_entropy(const float* logits, const int64_t* targets, size_t batch, size_t classes,
+                                size_t batch_total, float* loss, float* row_max, float* row_sum,
+                                double* partial) {
+    VC_API_BEGIN
+    ensure_init();
+    check_dims(batch, classes, 1);
+    if (batch_total == 0) batch_total = batch;
+    if (batch_total == 0) fail(VC_ERR_INVALID, "cross_entropy of an empty batch is undefined");
+    if (classes == 0) fail(VC_ERR_INVALID, "cross_entropy needs at least one class");
+    if (batch && (!logits || !targets)) fail(VC_ERR_INVALID, "cross_entropy: null pointer");
+    Scratch terms(batch * sizeof(float) + 16);
+    if (batch) {
+        RowArgs a{};
+        a.x = logits;
+        a.targets = reinterpret_cast<const long long*>(targets);
+        a.row_max = row_max;
+        a.row_sum = row_sum;
+        a.row_term = terms.as<float>();
+        launch_family<CE_FWD>(a, batch, classes, 1);
+    }
+    ce_finish_kernel<<<1, 1024, 0, stream()>>>(terms.as<float>(), batch, static_cast<float>(batch_total), loss,
+                                                partial);
+    check_launch("cross_entropy_finish");
+    VC_API_END
+}
+
+vc_status vc_cuda_cross_entropy_backward(const float* logits, const int64_t* targets, const float* row_max,
+                                         const float* row_sum, const float* upstream, size_t batch,
+                                         size_t classes, size_t batch_total, float* dlogits) {
+    VC_API_BEGIN
+    ensure_init();
+    check_dims(batch, classes, 1);
+    if (batch_total == 0) batch_total = batch;
+    if (!batch || !classes) return VC_OK;
+    if (!logits || !targets || !row_max || !row_sum || !upstream || !dlogits)
+        fail(VC_ERR_INVALID, "cross_entropy_backward: null pointer");
+    const bool vec = classes % 4 == 0 && aligned16(logits) && aligned16(dlogits);
+    const unsigned grid = static_cast<unsigned>(std::min<std::size_t>(batch, static_cast<std::size_t>(sm_count()) * 16));
+    const auto* t = reinterpret_cast<const long long*>(targets);
+    if (vec) ce_backward_kernel<true><<<grid, kThreads, 0, stream()>>>(logits, t, row_max, row_sum, upstream, batch, classes, static_cast<float>(batch_total), dlogits);
+    else ce_backward_kernel<false><<<grid, kThreads, 0, stream()>>>(logits, t, row_max, row_sum, upstream, batch, classes, static_cast<float>(batch_total), dlogits);
+    check_launch("cross_entropy_backward");
+    VC_API_END
+}
+
+}  // extern "C"

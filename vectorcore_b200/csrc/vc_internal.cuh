@@ -1,0 +1,211 @@
+// vc_internal.cuh -- shared host/device plumbing of the VectorCore CUDA device.
+#pragma once
+
+#include "vc_cuda.h"
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+namespace vc {
+
+// ---------------------------------------------------------------------------
+// Host-side error model. Internal code throws vc::Error; every extern "C"
+// entry point catches it (VC_API_BEGIN/END), records the message in a
+// thread-local string and returns the status.
+// ---------------------------------------------------------------------------
+struct Error : std::runtime_error {
+    vc_status status;
+    Error(vc_status s, const std::string& message) : std::runtime_error(message), status(s) {}
+};
+
+[[noreturn]] void fail(vc_status status, const std::string& message);
+void set_last_error(const std::string& message);
+void check_cuda(cudaError_t err, const char* what);
+
+#define VC_CUDA(expr) ::vc::check_cuda((expr), #expr)
+
+#define VC_API_BEGIN try {
+#define VC_API_END                                                   \
+    return VC_OK;                                                    \
+    }                                                                \
+    catch (const ::vc::Error& e) {                                   \
+        ::vc::set_last_error(e.what());                              \
+        return e.status;                                             \
+    }                                                                \
+    catch (const std::exception& e) {                                \
+        ::vc::set_last_error(e.what());                              \
+        return VC_ERR_RUNTIME;                                       \
+    }                                                                \
+    catch (...) {                                                    \
+        ::vc::set_last_error("unknown error in the VectorCore CUDA device"); \
+        return VC_ERR_RUNTIME;                                       \
+    }
+
+// ---------------------------------------------------------------------------
+// Runtime state (runtime.cu).
+// ---------------------------------------------------------------------------
+void ensure_init();              // init device 0 if nothing was selected yet
+cudaStream_t stream();           // the enqueue stream
+int sm_count();
+unsigned* counters();            // zeroed ticket counters (kCounterSlots)
+unsigned* device_error_word();   // sticky device error bits
+void check_launch(const char* what);
+
+constexpr std::size_t kCounterSlots = 1u << 16;
+
+// Device error bits (set with atomicOr by kernels, read at sync points).
+constexpr unsigned kErrWaitTimeout = 1u << 0;   // a bounded wait gave up
+constexpr unsigned kErrBadTarget = 1u << 1;     // class target out of range
+constexpr unsigned kErrBadIndex = 1u << 2;      // scatter index out of range
+
+// Stream-ordered scratch from the pool; returned to the pool on scope exit
+// (after the kernels that use it were enqueued, which stream order makes safe).
+class Scratch {
+public:
+    explicit Scratch(std::size_t bytes);
+    ~Scratch();
+    Scratch(const Scratch&) = delete;
+    Scratch& operator=(const Scratch&) = delete;
+    template <typename T> T* as() const { return static_cast<T*>(ptr_); }
+private:
+    void* ptr_{nullptr};
+};
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<std::uintptr_t>(p) & 15u) == 0; }
+
+inline unsigned grid_for(std::size_t work_items, unsigned threads, unsigned max_ctas_per_sm = 8) {
+    const std::size_t ctas = (work_items + threads - 1) / threads;
+    const std::size_t cap = static_cast<std::size_t>(sm_count()) * max_ctas_per_sm;
+    std::size_t g = ctas < cap ? ctas : cap;
+    return static_cast<unsigned>(g ? g : 1);
+}
+
+// ---------------------------------------------------------------------------
+// Device helpers.
+// ---------------------------------------------------------------------------
+
+// 32-bit division by a runtime-invariant divisor d >= 1 (Granlund-Montgomery,
+// round-up multiplier): with l = ceil(log2 d) and
+// mul = floor(2^32 * (2^l - d) / d) + 1, q = (umulhi(n, mul) + n) >> l for
+// every 32-bit n (the sum is formed in 64 bits).
+struct FastDiv {
+    unsigned divisor{1};
+    unsigned mul{1};
+    unsigned shift{0};
+    FastDiv() = default;
+    explicit FastDiv(unsigned d) : divisor(d) {
+        unsigned l = 0;
+        while ((1ull << l) < d) ++l;
+        mul = static_cast<unsigned>(((1ull << 32) * ((1ull << l) - d)) / d + 1);
+        shift = l;
+    }
+    __device__ __forceinline__ unsigned div(unsigned n) const {
+        const unsigned hi = __umulhi(n, mul);
+        return static_cast<unsigned>((static_cast<unsigned long long>(hi) + n) >> shift);
+    }
+    __device__ __forceinline__ void divmod(unsigned n, unsigned& q, unsigned& r) const {
+        q = div(n);
+        r = n - q * divisor;
+    }
+};
+
+__device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+__device__ __forceinline__ void st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+
+// Streaming (evict-first) variants for data touched once.
+__device__ __forceinline__ float4 ld4_stream(const float* p) {
+    float4 v;
+    asm volatile("ld.global.cs.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ void st4_stream(float* p, float4 v) {
+    asm volatile("st.global.cs.v4.f32 [%0], {%1,%2,%3,%4};"
+                 :: "l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w) : "memory");
+}
+
+// Max/argmax candidate under the reference's scan semantics: a larger value
+// wins; equal values (==, so -0 == +0) keep the smaller index; NaN is never
+// a candidate (the caller applies the "NaN at index 0 wins" rule).
+struct MaxCand {
+    float v;
+    long long i;  // -1: no candidate
+};
+
+__device__ __forceinline__ MaxCand max_combine(MaxCand a, MaxCand b) {
+    if (a.i < 0) return b;
+    if (b.i < 0) return a;
+    if (b.v > a.v) return b;
+    if (a.v > b.v) return a;
+    return b.i < a.i ? b : a;
+}
+
+__device__ __forceinline__ MaxCand max_take(MaxCand c, float v, long long i) {
+    // Elements of one thread arrive in increasing index order.
+    if (v != v) return c;  // NaN
+    if (c.i < 0 || v > c.v) return MaxCand{v, i};
+    return c;
+}
+
+__device__ __forceinline__ MaxCand shfl_xor_cand(MaxCand c, int mask) {
+    MaxCand o;
+    o.v = __shfl_xor_sync(0xffffffffu, c.v, mask);
+    o.i = __shfl_xor_sync(0xffffffffu, c.i, mask);
+    return o;
+}
+
+// Fixed-shape warp and block trees (the combine order depends only on the
+// thread index, so results do not depend on scheduling).
+__device__ __forceinline__ double warp_sum(double v) {
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+    return v;
+}
+
+__device__ __forceinline__ MaxCand warp_max(MaxCand c) {
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) c = max_combine(c, shfl_xor_cand(c, m));
+    return c;
+}
+
+// Block reductions over blockDim.x threads (multiple of 32, <= 1024). The
+// result is returned to every thread. `scratch` needs 32 entries.
+__device__ __forceinline__ double block_sum(double v, double* scratch) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    v = warp_sum(v);
+    __syncthreads();
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    double t = lane < nw ? scratch[lane] : 0.0;
+    t = warp_sum(t);
+    return t;
+}
+
+__device__ __forceinline__ MaxCand block_max(MaxCand c, float* sv, long long* si) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    c = warp_max(c);
+    __syncthreads();
+    if (lane == 0) { sv[warp] = c.v; si[warp] = c.i; }
+    __syncthreads();
+    MaxCand t = lane < nw ? MaxCand{sv[lane], si[lane]} : MaxCand{0.0f, -1};
+    return warp_max(t);
+}
+
+// ---------------------------------------------------------------------------
+// Shapes.
+// ---------------------------------------------------------------------------
+constexpr int kMaxRank = 8;
+
+struct ShapeView {
+    int rank{0};
+    std::size_t dims[kMaxRank]{};
+};
+
+std::size_t checked_numel(const size_t* shape, int rank);
+void validate_rank(int rank, const char* what);
+
+}  // namespace vc
