@@ -40,6 +40,12 @@ class OracleError(RuntimeError):
     pass
 
 
+def _c(a, dtype=np.float32):
+    """C-contiguous array of `dtype` that keeps 0-d shapes (np.ascontiguousarray
+    would promote them to 1-d)."""
+    return np.require(np.asarray(a, dtype), requirements="C")
+
+
 def _fp(a):
     if a is None:
         return None
@@ -85,8 +91,8 @@ class _Impl:
 
     # ---- elementwise --------------------------------------------------
     def binary(self, op, a, b):
-        a = np.ascontiguousarray(a, np.float32)
-        b = np.ascontiguousarray(b, np.float32)
+        a = _c(a)
+        b = _c(b)
         oshape = broadcast_shape(a.shape, b.shape)
         out = np.empty(oshape, np.float32)
         sa, ra = _shape(a.shape)
@@ -96,31 +102,31 @@ class _Impl:
         return out
 
     def unary(self, op, x):
-        x = np.ascontiguousarray(x, np.float32)
+        x = _c(x)
         out = np.empty_like(x)
         self._check(self._fn("unary")(op, _fp(x), _fp(out), ctypes.c_size_t(x.size)) or 0)
         return out
 
     def sum(self, x):
-        x = np.ascontiguousarray(x, np.float32)
+        x = _c(x)
         return np.float32(self._fn("sum")(_fp(x), ctypes.c_size_t(x.size)))
 
     def reduce_axis(self, op, x, outer, length, inner):
-        x = np.ascontiguousarray(x, np.float32)
+        x = _c(x)
         out = np.empty(outer * inner, np.float32)
         self._reduce_axis_call(op, x, out, outer, length, inner)
         return out
 
     def scatter_axis(self, values, indices, outer, length, inner):
-        values = np.ascontiguousarray(values, np.float32)
-        indices = np.ascontiguousarray(indices, np.float32)
+        values = _c(values)
+        indices = _c(indices)
         out = np.empty(outer * length * inner, np.float32)
         self._fn("scatter_axis")(_fp(values), _fp(indices), _fp(out), ctypes.c_size_t(outer),
                                  ctypes.c_size_t(length), ctypes.c_size_t(inner))
         return out
 
     def sum_to_shape(self, g, target):
-        g = np.ascontiguousarray(g, np.float32)
+        g = _c(g)
         out = np.empty(tuple(target), np.float32)
         sg, rg = _shape(g.shape)
         st, rt = _shape(target)
@@ -149,7 +155,7 @@ class Port(_Impl):
                                              ctypes.c_size_t(length), ctypes.c_size_t(inner)))
 
     def argmax_i64(self, x, outer, length, inner):
-        x = np.ascontiguousarray(x, np.float32)
+        x = _c(x)
         out = np.empty(outer * inner, np.float32)
         idx = np.empty(outer * inner, np.int64)
         self._check(self.lib.vco_reduce_axis(ARGMAX, _fp(x), _fp(out), idx.ctypes.data_as(_i64p),
@@ -158,9 +164,9 @@ class Port(_Impl):
         return idx
 
     def binary_backward(self, op, a, b, g, need_a=True, need_b=True):
-        a = np.ascontiguousarray(a, np.float32)
-        b = np.ascontiguousarray(b, np.float32)
-        g = np.ascontiguousarray(g, np.float32)
+        a = _c(a)
+        b = _c(b)
+        g = _c(g)
         da = np.empty(a.shape, np.float32) if need_a else None
         db = np.empty(b.shape, np.float32) if need_b else None
         sa, ra = _shape(a.shape)
@@ -170,15 +176,23 @@ class Port(_Impl):
         return da, db
 
     def unary_backward(self, op, x, g):
-        x = np.ascontiguousarray(x, np.float32)
-        g = np.ascontiguousarray(g, np.float32)
+        x = _c(x)
+        g = _c(g)
         y = self.unary(op, x)
         dx = np.empty_like(x)
         self.lib.vco_unary_backward(op, _fp(x), _fp(y), _fp(g), _fp(dx), ctypes.c_size_t(x.size))
         return dx
 
+    def unary_backward_saved(self, op, x, y, g):
+        """Backward rule given the forward input x and a caller-supplied
+        forward output y (so GPU and CPU use the same saved tensor)."""
+        x, y, g = (_c(v) for v in (x, y, g))
+        dx = np.empty_like(x)
+        self.lib.vco_unary_backward(op, _fp(x), _fp(y), _fp(g), _fp(dx), ctypes.c_size_t(x.size))
+        return dx
+
     def log_softmax(self, x, axis=-1, stats=False):
-        x = np.ascontiguousarray(x, np.float32)
+        x = _c(x)
         outer, length, inner = _split(x.shape, axis)
         out = np.empty_like(x)
         m = np.empty(outer * inner, np.float32)
@@ -188,7 +202,7 @@ class Port(_Impl):
         return (out, m, s) if stats else out
 
     def softmax(self, x, axis=-1):
-        x = np.ascontiguousarray(x, np.float32)
+        x = _c(x)
         outer, length, inner = _split(x.shape, axis)
         out = np.empty_like(x)
         self.lib.vco_softmax(_fp(x), _fp(out), ctypes.c_size_t(outer), ctypes.c_size_t(length),
@@ -196,8 +210,8 @@ class Port(_Impl):
         return out
 
     def log_softmax_backward(self, x, g, axis=-1):
-        x = np.ascontiguousarray(x, np.float32)
-        g = np.ascontiguousarray(g, np.float32)
+        x = _c(x)
+        g = _c(g)
         outer, length, inner = _split(x.shape, axis)
         dx = np.empty_like(x)
         self.lib.vco_log_softmax_backward(_fp(x), _fp(g), _fp(dx), ctypes.c_size_t(outer),
@@ -205,8 +219,8 @@ class Port(_Impl):
         return dx
 
     def softmax_backward(self, x, g, axis=-1):
-        x = np.ascontiguousarray(x, np.float32)
-        g = np.ascontiguousarray(g, np.float32)
+        x = _c(x)
+        g = _c(g)
         outer, length, inner = _split(x.shape, axis)
         dx = np.empty_like(x)
         self.lib.vco_softmax_backward(_fp(x), _fp(g), _fp(dx), ctypes.c_size_t(outer),
@@ -214,8 +228,8 @@ class Port(_Impl):
         return dx
 
     def cross_entropy(self, logits, targets, upstream=1.0, grad=True):
-        logits = np.ascontiguousarray(logits, np.float32)
-        targets = np.ascontiguousarray(targets, np.int64)
+        logits = _c(logits)
+        targets = _c(targets, np.int64)
         batch, classes = logits.shape
         loss = ctypes.c_float()
         dx = np.empty_like(logits) if grad else None
@@ -228,7 +242,7 @@ class Port(_Impl):
 
     def reduce_op(self, kind, x, axis=None, g=None):
         """kind: 'sum' | 'mean' | 'max'. Returns (out, dx or None)."""
-        x = np.ascontiguousarray(x, np.float32)
+        x = _c(x)
         k = {"sum": 0, "mean": 1, "max": 2}[kind]
         full = axis is None
         if full:
@@ -239,7 +253,7 @@ class Port(_Impl):
         out = np.empty(oshape, np.float32)
         dx = None
         if g is not None:
-            g = np.ascontiguousarray(g, np.float32).reshape(oshape)
+            g = _c(g).reshape(oshape)
             dx = np.empty_like(x)
         s, r = _shape(x.shape)
         self._check(self.lib.vco_reduce_op(k, _fp(x), s, r, int(full), ctypes.c_long(axis or 0),
@@ -266,9 +280,9 @@ class Reference(_Impl):
                                                ctypes.c_size_t(length), ctypes.c_size_t(inner)))
 
     def binary_backward(self, op, a, b, g, need_a=True, need_b=True):
-        a = np.ascontiguousarray(a, np.float32)
-        b = np.ascontiguousarray(b, np.float32)
-        g = np.ascontiguousarray(g, np.float32)
+        a = _c(a)
+        b = _c(b)
+        g = _c(g)
         da = np.empty(a.shape, np.float32) if need_a else None
         db = np.empty(b.shape, np.float32) if need_b else None
         sa, ra = _shape(a.shape)
@@ -278,19 +292,19 @@ class Reference(_Impl):
         return da, db
 
     def unary_backward(self, op, x, g):
-        x = np.ascontiguousarray(x, np.float32)
-        g = np.ascontiguousarray(g, np.float32)
+        x = _c(x)
+        g = _c(g)
         dx = np.empty_like(x)
         self._check(self.lib.vcref_unary_backward(op, _fp(x), ctypes.c_size_t(x.size), _fp(g),
                                                   None, _fp(dx)))
         return dx
 
     def _softmax(self, kind, x, axis, g=None):
-        x = np.ascontiguousarray(x, np.float32)
+        x = _c(x)
         out = np.empty_like(x)
         dx = None
         if g is not None:
-            g = np.ascontiguousarray(g, np.float32)
+            g = _c(g)
             dx = np.empty_like(x)
         s, r = _shape(x.shape)
         self._check(self.lib.vcref_softmax_op(kind, _fp(x), s, r, ctypes.c_long(axis), _fp(out),
@@ -310,8 +324,8 @@ class Reference(_Impl):
         return self._softmax(1, x, axis, g)[1]
 
     def cross_entropy(self, logits, targets, upstream=1.0, grad=True):
-        logits = np.ascontiguousarray(logits, np.float32)
-        targets = np.ascontiguousarray(targets, np.int64)
+        logits = _c(logits)
+        targets = _c(targets, np.int64)
         batch, classes = logits.shape
         loss = ctypes.c_float()
         dx = np.empty_like(logits) if grad else None
@@ -323,7 +337,7 @@ class Reference(_Impl):
         return np.float32(loss.value), dx
 
     def reduce_op(self, kind, x, axis=None, g=None):
-        x = np.ascontiguousarray(x, np.float32)
+        x = _c(x)
         k = {"sum": 0, "mean": 1, "max": 2, "argmax": 3}[kind]
         full = axis is None
         if full:
@@ -334,7 +348,7 @@ class Reference(_Impl):
         out = np.empty(oshape, np.float32)
         dx = None
         if g is not None:
-            g = np.ascontiguousarray(g, np.float32).reshape(oshape)
+            g = _c(g).reshape(oshape)
             dx = np.empty_like(x)
         s, r = _shape(x.shape)
         self._check(self.lib.vcref_reduce_op(k, _fp(x), s, r, int(full), ctypes.c_long(axis or 0),

@@ -65,13 +65,18 @@ def assert_sum_close(got, ref, n, rms, rtol=SUM_RTOL, what=""):
                            f"{float(np.max(err / np.maximum(scale, 1e-30))):.3e}")
 
 
-def assert_rel(got, ref, rtol=SUM_RTOL, what=""):
-    """|got - ref| <= rtol * (|ref| + 1e-3 * max|ref|): relative, with a floor
-    for entries far below the array's scale."""
+def assert_rel(got, ref, rtol=SUM_RTOL, what="", scale=None):
+    """|got - ref| <= rtol * (|ref| + floor): relative, with a floor for
+    entries far below the scale of the terms that produced them. The floor is
+    1e-3 * max|ref|, or 0.1 * `scale` when given -- backward results are sums
+    g + de*e whose terms have the magnitude of the upstream gradient, so a
+    near-cancellation leaves an absolute error of a few ulp of `scale`."""
     got = np.asarray(got, np.float64)
     ref = np.asarray(ref, np.float64)
     both_nan = np.isnan(got) & np.isnan(ref)
     floor = 1e-3 * (np.max(np.abs(ref[np.isfinite(ref)])) if np.isfinite(ref).any() else 0.0)
+    if scale is not None:
+        floor = max(floor, 0.1 * float(scale))
     err = np.where(both_nan, 0.0, np.abs(got - ref))
     bad = err > rtol * (np.abs(ref) + floor)
     assert not bad.any(), (f"{what}: {int(bad.sum())} of {got.size} outside rtol {rtol}; worst abs err "

@@ -40,10 +40,14 @@ __device__ __forceinline__ float uop(float x) {
     else if constexpr (OP == VC_RELU) return x > 0.0f ? x : 0.0f;
     else if constexpr (OP == VC_RELU_GRAD) return x > 0.0f ? 1.0f : 0.0f;
     else if constexpr (OP == VC_SIGMOID) {
-        // Branchy form of cpu_backend.cpp:302-307 (keeps exp from overflowing).
-        if (x >= 0.0f) return 1.0f / (1.0f + expf(-x));
-        const float e = expf(x);
-        return e / (1.0f + e);
+        // cpu_backend.cpp:302-307 computes 1/(1+exp(-x)) for x >= 0 and
+        // e/(1+e) with e = exp(x) otherwise. Both branches evaluate
+        // exp(-|x|), so selecting the numerator gives the same bits with one
+        // expf and one division and no warp divergence (NaN takes the second
+        // form, as in the reference).
+        const float e = expf(-fabsf(x));
+        const float num = x >= 0.0f ? 1.0f : e;
+        return num / (1.0f + e);
     } else if constexpr (OP == VC_EXP) return expf(x);
     else return logf(x);
 }
