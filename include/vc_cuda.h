@@ -268,6 +268,20 @@ vc_status vc_cuda_cross_entropy_backward(const float* logits, const int64_t* tar
                                          const float* upstream, size_t batch, size_t classes,
                                          size_t batch_total, float* dlogits);
 
+/* ---- existing ops (correct, not tuned: off the bandwidth-bound path) ---- */
+
+/* Batched out[z] (m x n) = op(A)[a_offsets[z]..] @ op(B)[b_offsets[z]..];
+ * with trans_a A is stored (k x m), with trans_b B is stored (n x k); offsets
+ * in elements, host arrays of `batch` entries. Replaces MetalBackend::matmul
+ * (metal_backend.hpp:33-37) and cpu::matmul (cpu_backend.cpp:318-366). */
+vc_status vc_cuda_matmul(const float* a, const float* b, float* out, size_t m, size_t k, size_t n,
+                         const size_t* a_offsets, const size_t* b_offsets, size_t batch,
+                         int trans_a, int trans_b);
+
+/* Swap the last two axes of a contiguous [batch, rows, cols] tensor.
+ * Replaces MetalBackend::transpose_last2 (metal_backend.hpp:38-39). */
+vc_status vc_cuda_transpose_last2(const float* in, float* out, size_t batch, size_t rows, size_t cols);
+
 #ifdef __cplusplus
 }
 #endif

@@ -25,7 +25,7 @@ HEADER = _build.INCLUDE / "vc_cuda.h"
 if not LIB_PATH.exists():
     raise ImportError(
         f"vectorcore_b200: the CUDA device library {LIB_PATH} is not built; run "
-        "`python -m vectorcore_b200.build` (nvcc for sm_100a). There is no CPU fallback.")
+        "`python vectorcore_b200/build.py` (nvcc for sm_100a). There is no CPU fallback.")
 
 lib = ctypes.CDLL(str(LIB_PATH))
 
@@ -99,6 +99,8 @@ _SIGS = {
     "vc_cuda_softmax_backward": (c_int, [_f, _f, _f, _f, _f, c_size_t, c_size_t, c_size_t]),
     "vc_cuda_cross_entropy": (c_int, [_f, c_void_p, c_size_t, c_size_t, c_size_t, _f, _f, _f, c_void_p]),
     "vc_cuda_cross_entropy_backward": (c_int, [_f, c_void_p, _f, _f, _f, c_size_t, c_size_t, c_size_t, _f]),
+    "vc_cuda_matmul": (c_int, [_f, _f, _f, c_size_t, c_size_t, c_size_t, _szp, _szp, c_size_t, c_int, c_int]),
+    "vc_cuda_transpose_last2": (c_int, [_f, _f, c_size_t, c_size_t, c_size_t]),
 }
 
 

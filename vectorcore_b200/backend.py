@@ -163,6 +163,23 @@ class CudaBackend:
     def axpy_inplace(self, target, source, count, alpha) -> None:
         _abi.call("vc_cuda_axpy", _p(target), _p(source), ctypes.c_size_t(count), ctypes.c_float(alpha))
 
+    def matmul(self, a, b, m, k, n, a_offsets, b_offsets, trans_a=False, trans_b=False) -> CudaStorage:
+        if len(a_offsets) != len(b_offsets) or not a_offsets:
+            raise ValueError("matmul needs one A and B offset per batch")
+        batch = len(a_offsets)
+        out = CudaStorage(batch * m * n)
+        ao = (ctypes.c_size_t * batch)(*[int(v) for v in a_offsets])
+        bo = (ctypes.c_size_t * batch)(*[int(v) for v in b_offsets])
+        _abi.call("vc_cuda_matmul", _p(a), _p(b), _p(out), ctypes.c_size_t(m), ctypes.c_size_t(k),
+                  ctypes.c_size_t(n), ao, bo, ctypes.c_size_t(batch), int(trans_a), int(trans_b))
+        return out
+
+    def transpose_last2(self, inp, batch, rows, cols) -> CudaStorage:
+        out = CudaStorage(batch * rows * cols)
+        _abi.call("vc_cuda_transpose_last2", _p(inp), _p(out), ctypes.c_size_t(batch), ctypes.c_size_t(rows),
+                  ctypes.c_size_t(cols))
+        return out
+
     # ---- fused entry points of the CUDA device ---------------------------------------
     def fill(self, count, value) -> CudaStorage:
         out = CudaStorage(count)

@@ -1,7 +1,9 @@
 """Build the VectorCore CUDA device library for sm_100a (B200).
 
-    python -m vectorcore_b200.build          # -> vectorcore_b200/_lib/libvc_cuda.so
+    python vectorcore_b200/build.py          # -> vectorcore_b200/_lib/libvc_cuda.so
 
+(run by path, not with -m: importing the package loads the library, which
+may not exist yet). 
 nvcc compiles every ``csrc/*.cu`` for ``sm_100a`` only (no PTX for other
 targets), with ``-fmad=false`` (no contraction of a*b+c, so elementwise results
 match the reference's CPU arithmetic bit for bit) and IEEE division / square

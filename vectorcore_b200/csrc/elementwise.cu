@@ -124,7 +124,11 @@ binary_flat_kernel(const float* __restrict__ a, const float* __restrict__ b,
 // CTA streams the TR*L tile elements.
 // ---------------------------------------------------------------------------
 constexpr int kTileRowsMax = 256;
+constexpr unsigned kTileElems = 4096;   // output elements per tile
 
+// Tile t covers rows [rt * tile_rows, +tile_rows) and, when a row is longer
+// than a tile, the column chunk [cc * chunk, +chunk) of a single row
+// (t = rt * col_chunks + cc), so long rows spread over many CTAs.
 struct BcastDesc {
     int lead_rank;                      // collapsed leading dims (row decode)
     std::size_t lead_dims[kMaxRank];
@@ -132,24 +136,26 @@ struct BcastDesc {
     long long b_lead[kMaxRank];
     long long a_inner, b_inner;         // stride along the row (0 or any)
     std::size_t rows, L;
-    unsigned tile_rows;
+    unsigned tile_rows;                 // > 1 only when L < kTileElems (then col_chunks == 1)
+    std::size_t chunk, col_chunks;
     FastDiv div_L;
 };
 
 template <int OP, bool VEC>
 __global__ void __launch_bounds__(kThreads)
 binary_tiled_kernel(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ out,
-                    const BcastDesc d, const float* __restrict__ sa, const float* __restrict__ sb,
-                    float av, float bv) {
+                    const BcastDesc d, float av, float bv) {
     __shared__ long long s_aoff[kTileRowsMax];
     __shared__ long long s_boff[kTileRowsMax];
     // A by-value operand is encoded as a null pointer with all strides 0.
-    const float a_const = sa ? __ldg(sa) : av;
-    const float b_const = sb ? __ldg(sb) : bv;
-    const std::size_t tiles = (d.rows + d.tile_rows - 1) / d.tile_rows;
+    const std::size_t row_tiles = (d.rows + d.tile_rows - 1) / d.tile_rows;
+    const std::size_t tiles = row_tiles * d.col_chunks;
     for (std::size_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-        const std::size_t row0 = tile * d.tile_rows;
+        const std::size_t rt = tile / d.col_chunks, cc = tile - rt * d.col_chunks;
+        const std::size_t row0 = rt * d.tile_rows;
+        const std::size_t c0 = cc * d.chunk;
         const unsigned nrows = static_cast<unsigned>(min(static_cast<std::size_t>(d.tile_rows), d.rows - row0));
+        const unsigned clen = static_cast<unsigned>(min(d.chunk, d.L - c0));
         if (threadIdx.x < nrows) {
             std::size_t r = row0 + threadIdx.x;
             long long ao = 0, bo = 0;
@@ -160,36 +166,55 @@ binary_tiled_kernel(const float* __restrict__ a, const float* __restrict__ b, fl
                 ao += static_cast<long long>(c) * d.a_lead[k];
                 bo += static_cast<long long>(c) * d.b_lead[k];
             }
-            s_aoff[threadIdx.x] = ao;
-            s_boff[threadIdx.x] = bo;
+            s_aoff[threadIdx.x] = ao + static_cast<long long>(c0) * d.a_inner;
+            s_boff[threadIdx.x] = bo + static_cast<long long>(c0) * d.b_inner;
         }
         __syncthreads();
-        const unsigned tile_elems = nrows * static_cast<unsigned>(d.L);
-        float* tile_out = out + row0 * d.L;
+        const unsigned tile_elems = nrows * clen;
+        float* tile_out = out + row0 * d.L + c0;
         if constexpr (VEC) {
             for (unsigned e = threadIdx.x * 4; e < tile_elems; e += kThreads * 4) {
-                unsigned row, col;
-                d.div_L.divmod(e, row, col);
+                unsigned row = 0, col = e;
+                if (nrows > 1) d.div_L.divmod(e, row, col);
                 float4 x, y;
-                if (!a) x = make_float4(a_const, a_const, a_const, a_const);
+                if (!a) x = make_float4(av, av, av, av);
                 else if (d.a_inner == 0) { const float v = __ldg(a + s_aoff[row]); x = make_float4(v, v, v, v); }
                 else x = ldg4(a + s_aoff[row] + col);
-                if (!b) y = make_float4(b_const, b_const, b_const, b_const);
+                if (!b) y = make_float4(bv, bv, bv, bv);
                 else if (d.b_inner == 0) { const float v = __ldg(b + s_boff[row]); y = make_float4(v, v, v, v); }
                 else y = ldg4(b + s_boff[row] + col);
-                st4_stream(tile_out + e, bop4<OP>(x, y));
+                st4_stream(tile_out + static_cast<std::size_t>(row) * d.L + col, bop4<OP>(x, y));
             }
         } else {
             for (unsigned e = threadIdx.x; e < tile_elems; e += kThreads) {
-                unsigned row, col;
-                d.div_L.divmod(e, row, col);
-                const float x = a ? __ldg(a + s_aoff[row] + static_cast<long long>(col) * d.a_inner) : a_const;
-                const float y = b ? __ldg(b + s_boff[row] + static_cast<long long>(col) * d.b_inner) : b_const;
-                tile_out[e] = bop<OP>(x, y);
+                unsigned row = 0, col = e;
+                if (nrows > 1) d.div_L.divmod(e, row, col);
+                const float x = a ? __ldg(a + s_aoff[row] + static_cast<long long>(col) * d.a_inner) : av;
+                const float y = b ? __ldg(b + s_boff[row] + static_cast<long long>(col) * d.b_inner) : bv;
+                tile_out[static_cast<std::size_t>(row) * d.L + col] = bop<OP>(x, y);
             }
         }
         __syncthreads();
     }
+}
+
+// Both operands constant over the whole output (e.g. the 0-d gradient of a
+// sum broadcast back): every element is op(a0, b0).
+template <int OP>
+__global__ void __launch_bounds__(kThreads)
+binary_splat_kernel(const float* __restrict__ ap, float av, const float* __restrict__ bp, float bv,
+                    float* __restrict__ out, std::size_t n, bool vec) {
+    const float v = bop<OP>(ap ? __ldg(ap) : av, bp ? __ldg(bp) : bv);
+    const std::size_t tid = static_cast<std::size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const std::size_t stride = static_cast<std::size_t>(gridDim.x) * blockDim.x;
+    std::size_t start = 0;
+    if (vec) {
+        const std::size_t n4 = n >> 2;
+        const float4 v4 = make_float4(v, v, v, v);
+        for (std::size_t i = tid; i < n4; i += stride) st4_stream(out + i * 4, v4);
+        start = n4 * 4;
+    }
+    for (std::size_t k = start + tid; k < n; k += stride) out[k] = v;
 }
 
 // ---------------------------------------------------------------------------
@@ -370,6 +395,16 @@ static void launch_binary_op(const Operand& a, const Operand& b, float* out, con
         check_launch("binary_flat");
         return;
     }
+    // Both operands constant everywhere: splat.
+    bool all_zero = true;
+    for (int i = 0; i < c.rank; ++i) all_zero = all_zero && c.sa[i] == 0 && c.sb[i] == 0;
+    if (all_zero) {
+        const bool vec = aligned16(out);
+        binary_splat_kernel<OP><<<grid_for(vec ? (n + 3) / 4 : n, kThreads), kThreads, 0, s>>>(
+            a.ptr, a.value, b.ptr, b.value, out, n, vec);
+        check_launch("binary_splat");
+        return;
+    }
     // Tiled strided path.
     BcastDesc d{};
     const int r = c.rank;  // >= 1 here
@@ -384,10 +419,17 @@ static void launch_binary_op(const Operand& a, const Operand& b, float* out, con
         d.b_lead[i] = c.sb[i];
         d.rows *= c.dims[i];
     }
-    if (d.L > (1u << 30)) fail(VC_ERR_OVERFLOW, "broadcast inner run longer than 2^30 elements");
-    const std::size_t want = std::max<std::size_t>(1, 4096 / d.L);
-    d.tile_rows = static_cast<unsigned>(std::min<std::size_t>({want, static_cast<std::size_t>(kTileRowsMax), d.rows}));
-    d.div_L = FastDiv(static_cast<unsigned>(d.L));
+    if (d.L >= kTileElems) {
+        d.tile_rows = 1;
+        d.chunk = kTileElems;
+        d.col_chunks = (d.L + kTileElems - 1) / kTileElems;
+    } else {
+        d.tile_rows = static_cast<unsigned>(std::min<std::size_t>({kTileElems / d.L,
+                                                                   static_cast<std::size_t>(kTileRowsMax), d.rows}));
+        d.chunk = d.L;
+        d.col_chunks = 1;
+        d.div_L = FastDiv(static_cast<unsigned>(d.L));
+    }
     auto lead_ok = [&](const long long* lead, long long inner, const float* p) {
         if (!p || inner == 0) return true;
         if (inner != 1 || !aligned16(p)) return false;
@@ -397,10 +439,10 @@ static void launch_binary_op(const Operand& a, const Operand& b, float* out, con
     };
     const bool vec = d.L % 4 == 0 && aligned16(out) && lead_ok(d.a_lead, d.a_inner, a.ptr) &&
                      lead_ok(d.b_lead, d.b_inner, b.ptr);
-    const std::size_t tiles = (d.rows + d.tile_rows - 1) / d.tile_rows;
+    const std::size_t tiles = (d.rows + d.tile_rows - 1) / d.tile_rows * d.col_chunks;
     const unsigned grid = static_cast<unsigned>(std::min<std::size_t>(tiles, static_cast<std::size_t>(sm_count()) * 8));
-    if (vec) binary_tiled_kernel<OP, true><<<grid, kThreads, 0, s>>>(a.ptr, b.ptr, out, d, nullptr, nullptr, a.value, b.value);
-    else binary_tiled_kernel<OP, false><<<grid, kThreads, 0, s>>>(a.ptr, b.ptr, out, d, nullptr, nullptr, a.value, b.value);
+    if (vec) binary_tiled_kernel<OP, true><<<grid, kThreads, 0, s>>>(a.ptr, b.ptr, out, d, a.value, b.value);
+    else binary_tiled_kernel<OP, false><<<grid, kThreads, 0, s>>>(a.ptr, b.ptr, out, d, a.value, b.value);
     check_launch("binary_tiled");
 }
 
@@ -417,6 +459,16 @@ static void launch_binary(int op, const Operand& a, const Operand& b, float* out
         case VC_DIV: return launch_binary_op<VC_DIV>(a, b, out, c, n);
         default: fail(VC_ERR_INVALID, "unknown binary operation");
     }
+}
+
+// x + (-0.0f) == x for every float (including -0, +0 and NaN payload class),
+// so this is an exact broadcast copy built on the tiled path.
+void broadcast_copy(const float* src, const size_t* src_shape, int src_rank, float* out,
+                    const size_t* out_shape, int out_rank) {
+    const Operand s = align_operand(src, src_shape, nullptr, src_rank, out_shape, out_rank, "broadcast");
+    Operand minus_zero;
+    minus_zero.value = -0.0f;
+    launch_binary(VC_ADD, s, minus_zero, out, out_shape, out_rank);
 }
 
 template <int OP>

@@ -28,7 +28,17 @@ constexpr unsigned kThreads = 256;
 // segments (a constant, so the split depends on the problem size alone).
 constexpr unsigned long long kTargetThreads = 1ull << 18;
 constexpr unsigned long long kMinSegment = 16;         // reduced positions per segment (column)
-constexpr unsigned long long kRowChunk = 1ull << 16;   // elements per segment (row)
+constexpr unsigned long long kRowTargetCtas = 1024;    // aim for this many (row, segment) CTAs
+constexpr unsigned long long kRowMinSegment = 4096;    // elements per row segment, at least
+
+// Segments per row for a ROW-layout reduction of K rows of W elements: enough
+// (row, segment) CTAs to fill the machine, each at least kRowMinSegment long.
+// A function of the shape only.
+inline unsigned long long row_segments(unsigned long long K, unsigned long long W) {
+    unsigned long long S = (kRowTargetCtas + K - 1) / K;
+    S = std::min<unsigned long long>(S, (W + kRowMinSegment - 1) / kRowMinSegment);
+    return std::max<unsigned long long>(1, std::min<unsigned long long>(S, 65535));
+}
 
 // Element functions of the backward rules, arithmetic exactly as written in
 // src/ops.cpp: p, q are the other operands broadcast to the output shape.
@@ -122,22 +132,8 @@ reduce_col_kernel(const float* __restrict__ g, const float* __restrict__ p, cons
         double acc[V];
 #pragma unroll
         for (int v = 0; v < V; ++v) acc[v] = 0.0;
-        for (unsigned long long r = r0; r < r1; ++r) {
-            if constexpr (VEC) {
-                const float4 gv = load4(g, base[0] + off[0], d.is[0], i0);
-                const float4 pv = NOPS > 1 ? load4(p, base[1] + off[1], d.is[1], i0) : gv;
-                const float4 qv = NOPS > 2 ? load4(q, base[2] + off[2], d.is[2], i0) : gv;
-                acc[0] += vjp<F>(gv.x, pv.x, qv.x);
-                acc[1] += vjp<F>(gv.y, pv.y, qv.y);
-                acc[2] += vjp<F>(gv.z, pv.z, qv.z);
-                acc[3] += vjp<F>(gv.w, pv.w, qv.w);
-            } else {
-                const float gv = __ldg(g + base[0] + off[0] + static_cast<long long>(i0) * d.is[0]);
-                const float pv = NOPS > 1 ? __ldg(p + base[1] + off[1] + static_cast<long long>(i0) * d.is[1]) : gv;
-                const float qv = NOPS > 2 ? __ldg(q + base[2] + off[2] + static_cast<long long>(i0) * d.is[2]) : gv;
-                acc[0] += vjp<F>(gv, pv, qv);
-            }
-            // advance the reduced coordinate (row-major carry)
+        // advance the reduced coordinate by one position (row-major carry)
+        auto advance = [&]() {
             for (int k = d.nr - 1; k >= 0; --k) {
                 off[0] += d.rs[0][k];
                 off[1] += d.rs[1][k];
@@ -148,6 +144,50 @@ reduce_col_kernel(const float* __restrict__ g, const float* __restrict__ p, cons
                 off[1] -= d.rs[1][k] * static_cast<long long>(d.rdims[k]);
                 off[2] -= d.rs[2][k] * static_cast<long long>(d.rdims[k]);
             }
+        };
+        auto fetch = [&](const long long o[3]) -> float4 {
+            if constexpr (VEC) {
+                const float4 gv = load4(g, base[0] + o[0], d.is[0], i0);
+                const float4 pv = NOPS > 1 ? load4(p, base[1] + o[1], d.is[1], i0) : gv;
+                const float4 qv = NOPS > 2 ? load4(q, base[2] + o[2], d.is[2], i0) : gv;
+                return make_float4(vjp<F>(gv.x, pv.x, qv.x), vjp<F>(gv.y, pv.y, qv.y), vjp<F>(gv.z, pv.z, qv.z),
+                                   vjp<F>(gv.w, pv.w, qv.w));
+            } else {
+                const long long ii = static_cast<long long>(i0);
+                const float gv = __ldg(g + base[0] + o[0] + ii * d.is[0]);
+                const float pv = NOPS > 1 ? __ldg(p + base[1] + o[1] + ii * d.is[1]) : gv;
+                const float qv = NOPS > 2 ? __ldg(q + base[2] + o[2] + ii * d.is[2]) : gv;
+                return make_float4(vjp<F>(gv, pv, qv), 0.f, 0.f, 0.f);
+            }
+        };
+        auto accumulate = [&](float4 v) {
+            acc[0] += static_cast<double>(v.x);
+            if constexpr (VEC) {
+                acc[1] += static_cast<double>(v.y);
+                acc[2] += static_cast<double>(v.z);
+                acc[3] += static_cast<double>(v.w);
+            }
+        };
+        unsigned long long r = r0;
+        // four reduced positions in flight, accumulated in order
+        for (; r + 3 < r1; r += 4) {
+            long long o0[3] = {off[0], off[1], off[2]};
+            advance();
+            long long o1[3] = {off[0], off[1], off[2]};
+            advance();
+            long long o2[3] = {off[0], off[1], off[2]};
+            advance();
+            long long o3[3] = {off[0], off[1], off[2]};
+            advance();
+            const float4 v0 = fetch(o0), v1 = fetch(o1), v2 = fetch(o2), v3 = fetch(o3);
+            accumulate(v0);
+            accumulate(v1);
+            accumulate(v2);
+            accumulate(v3);
+        }
+        for (; r < r1; ++r) {
+            accumulate(fetch(off));
+            advance();
         }
         const unsigned long long o = ko * d.inner + i0;
         if (d.S == 1) {
@@ -180,12 +220,51 @@ reduce_col_finish(const double* __restrict__ partial, unsigned S, unsigned long 
 // ROW layout. Each output k reduces W = R * inner elements (e = r*inner + l).
 // grid = (min(K, 65535) rows, S segments of d.seg elements).
 // ---------------------------------------------------------------------------
+// The VJP values of the element group at reduced position e (4 lanes when
+// VEC, else lane x only).
+template <int F, bool VEC, bool HAS_R>
+__device__ __forceinline__ float4 row_fetch(const float* __restrict__ g, const float* __restrict__ p,
+                                            const float* __restrict__ q, const RedDesc& d, const long long base[3],
+                                            unsigned long long e) {
+    constexpr int NOPS = operands<F>();
+    long long off[3] = {0, 0, 0};
+    unsigned long long l = e;
+    if constexpr (HAS_R) {
+        const unsigned long long r = e / d.inner;
+        l = e - r * d.inner;
+        decode(r, d.nr, d.rdims, d.rs, off, nullptr);
+    }
+    if constexpr (VEC) {
+        const float4 gv = load4(g, base[0] + off[0], d.is[0], l);
+        const float4 pv = NOPS > 1 ? load4(p, base[1] + off[1], d.is[1], l) : gv;
+        const float4 qv = NOPS > 2 ? load4(q, base[2] + off[2], d.is[2], l) : gv;
+        return make_float4(vjp<F>(gv.x, pv.x, qv.x), vjp<F>(gv.y, pv.y, qv.y), vjp<F>(gv.z, pv.z, qv.z),
+                           vjp<F>(gv.w, pv.w, qv.w));
+    } else {
+        const long long li = static_cast<long long>(l);
+        const float gv = __ldg(g + base[0] + off[0] + li * d.is[0]);
+        const float pv = NOPS > 1 ? __ldg(p + base[1] + off[1] + li * d.is[1]) : gv;
+        const float qv = NOPS > 2 ? __ldg(q + base[2] + off[2] + li * d.is[2]) : gv;
+        return make_float4(vjp<F>(gv, pv, qv), 0.f, 0.f, 0.f);
+    }
+}
+
+template <bool VEC>
+__device__ __forceinline__ void row_accumulate(double& acc0, double& acc1, float4 v) {
+    if constexpr (VEC) {
+        acc0 += static_cast<double>(v.x) + static_cast<double>(v.y);
+        acc1 += static_cast<double>(v.z) + static_cast<double>(v.w);
+    } else {
+        acc0 += static_cast<double>(v.x);
+    }
+}
+
 template <int F, bool VEC, bool HAS_R>
 __global__ void __launch_bounds__(kThreads)
 reduce_row_kernel(const float* __restrict__ g, const float* __restrict__ p, const float* __restrict__ q,
                   const RedDesc d, float* __restrict__ out, double* __restrict__ partial) {
     constexpr int V = VEC ? 4 : 1;
-    constexpr int NOPS = operands<F>();
+    constexpr unsigned long long STEP = static_cast<unsigned long long>(kThreads) * V;
     __shared__ double s_red[32];
     const unsigned long long W = d.R * d.inner;
     const unsigned s = blockIdx.y;
@@ -195,28 +274,19 @@ reduce_row_kernel(const float* __restrict__ g, const float* __restrict__ p, cons
         long long base[3];
         decode(k, d.nk, d.kdims, d.ks, base, nullptr);
         double acc0 = 0.0, acc1 = 0.0;
-        for (unsigned long long e = e0 + threadIdx.x * V; e < e1; e += kThreads * V) {
-            long long off[3] = {0, 0, 0};
-            unsigned long long l = e;
-            if constexpr (HAS_R) {
-                const unsigned long long r = e / d.inner;
-                l = e - r * d.inner;
-                decode(r, d.nr, d.rdims, d.rs, off, nullptr);
-            }
-            if constexpr (VEC) {
-                const float4 gv = load4(g, base[0] + off[0], d.is[0], l);
-                const float4 pv = NOPS > 1 ? load4(p, base[1] + off[1], d.is[1], l) : gv;
-                const float4 qv = NOPS > 2 ? load4(q, base[2] + off[2], d.is[2], l) : gv;
-                acc0 += static_cast<double>(vjp<F>(gv.x, pv.x, qv.x)) + static_cast<double>(vjp<F>(gv.y, pv.y, qv.y));
-                acc1 += static_cast<double>(vjp<F>(gv.z, pv.z, qv.z)) + static_cast<double>(vjp<F>(gv.w, pv.w, qv.w));
-            } else {
-                const long long li = static_cast<long long>(l);
-                const float gv = __ldg(g + base[0] + off[0] + li * d.is[0]);
-                const float pv = NOPS > 1 ? __ldg(p + base[1] + off[1] + li * d.is[1]) : gv;
-                const float qv = NOPS > 2 ? __ldg(q + base[2] + off[2] + li * d.is[2]) : gv;
-                acc0 += vjp<F>(gv, pv, qv);
-            }
+        unsigned long long e = e0 + threadIdx.x * V;
+        // four independent groups in flight per thread
+        for (; e + 3 * STEP < e1; e += 4 * STEP) {
+            const float4 v0 = row_fetch<F, VEC, HAS_R>(g, p, q, d, base, e);
+            const float4 v1 = row_fetch<F, VEC, HAS_R>(g, p, q, d, base, e + STEP);
+            const float4 v2 = row_fetch<F, VEC, HAS_R>(g, p, q, d, base, e + 2 * STEP);
+            const float4 v3 = row_fetch<F, VEC, HAS_R>(g, p, q, d, base, e + 3 * STEP);
+            row_accumulate<VEC>(acc0, acc1, v0);
+            row_accumulate<VEC>(acc0, acc1, v1);
+            row_accumulate<VEC>(acc0, acc1, v2);
+            row_accumulate<VEC>(acc0, acc1, v3);
         }
+        for (; e < e1; e += STEP) row_accumulate<VEC>(acc0, acc1, row_fetch<F, VEC, HAS_R>(g, p, q, d, base, e));
         const double total = block_sum(acc0 + acc1, s_red);
         if (threadIdx.x == 0) {
             if (d.S == 1) out[k] = round_out(total, d.divisor);
@@ -278,6 +348,31 @@ static void launch_vjp_reduce(const Src ops[3], const size_t* src_shape, int src
         if (td != sd && td != 1) fail(VC_ERR_INVALID, "sum_to_shape: cannot reduce the gradient to the target shape");
         cls[i] = sd == 1 ? 0 : (td == 1 ? 2 : 1);
         if (cls[i] == 1) outsz *= sd;
+    }
+    // 1b. A kept dim along which every operand is constant (stride 0) gives
+    // the same result at every index: reduce on the compact shape without it
+    // and broadcast the result (e.g. the gradient of a * b for the scalar
+    // upstream of sum(): 2^32 products collapse to 2^17). Same values,
+    // bit for bit: each output sums the same products in the same order.
+    if (outsz > 0) {
+        bool any = false;
+        size_t c_src[kMaxRank], c_tgt[kMaxRank], full_tgt[kMaxRank];
+        for (int i = 0; i < src_rank; ++i) {
+            bool inv = cls[i] == 1;
+            for (int k = 0; k < operands<F>(); ++k) inv = inv && ops[k].st[i] == 0;
+            any = any || inv;
+            full_tgt[i] = i < lead ? 1 : t_shape[i - lead];
+            c_src[i] = inv ? 1 : src_shape[i];
+            c_tgt[i] = inv ? 1 : full_tgt[i];
+        }
+        if (any) {
+            std::size_t csz = 1;
+            for (int i = 0; i < src_rank; ++i) csz *= c_tgt[i];
+            Scratch compact(csz * sizeof(float));
+            launch_vjp_reduce<F>(ops, c_src, src_rank, c_tgt, src_rank, compact.as<float>(), divisor);
+            broadcast_copy(compact.as<float>(), c_tgt, src_rank, out, full_tgt, src_rank);
+            return;
+        }
     }
     // 2. merge neighbours of the same class that are contiguous for every operand.
     struct Dim { int cls; unsigned long long size; long long st[3]; };
@@ -379,9 +474,7 @@ static void launch_vjp_reduce(const Src ops[3], const size_t* src_shape, int src
         for (int i = 0; i < d.nr; ++i) vec = vec && d.rs[k][i] % 4 == 0;
     }
     const unsigned long long W = d.R * d.inner;
-    unsigned long long S = (W + kRowChunk - 1) / kRowChunk;
-    S = std::max<unsigned long long>(S, 1);
-    S = std::min<unsigned long long>(S, 65535);
+    unsigned long long S = row_segments(d.K, W);
     unsigned long long seg = (W + S - 1) / S;
     seg = (seg + 3) / 4 * 4;  // keep float4 groups inside one segment
     d.seg = seg;
@@ -415,38 +508,62 @@ static void vjp_reduce(int f, const Src ops[3], const size_t* src_shape, int src
 // Same-shape binary backward: both gradients in one pass (20 B/elem for mul
 // and div: read g, a, b; write da, db).
 // ---------------------------------------------------------------------------
+template <int OP>
+__device__ __forceinline__ void bb_one(float av, float bv, float gv, float& ga, float& gb) {
+    if constexpr (OP == VC_ADD) { ga = gv; gb = gv; }
+    else if constexpr (OP == VC_SUB) { ga = gv; gb = -gv; }
+    else if constexpr (OP == VC_MUL) { ga = vjp<V_MUL>(gv, bv, 0.f); gb = vjp<V_MUL>(gv, av, 0.f); }
+    else { ga = vjp<V_DIV_A>(gv, bv, 0.f); gb = vjp<V_DIV_B>(gv, av, bv); }
+}
+
+template <int OP>
+__device__ __forceinline__ void bb_four(const float4& av, const float4& bv, const float4& gv, float4& ga, float4& gb) {
+    bb_one<OP>(av.x, bv.x, gv.x, ga.x, gb.x);
+    bb_one<OP>(av.y, bv.y, gv.y, ga.y, gb.y);
+    bb_one<OP>(av.z, bv.z, gv.z, ga.z, gb.z);
+    bb_one<OP>(av.w, bv.w, gv.w, ga.w, gb.w);
+}
+
+// Two float4 of each input in flight per thread per iteration; at most 64
+// registers so four CTAs stay resident per SM.
 template <int OP, bool VEC>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 4)
 binary_backward_flat(const float* __restrict__ a, const float* __restrict__ b, const float* __restrict__ g,
                      float* __restrict__ da, float* __restrict__ db, std::size_t n) {
     const std::size_t stride = static_cast<std::size_t>(gridDim.x) * blockDim.x;
     const std::size_t tid = static_cast<std::size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    auto one = [&](float av, float bv, float gv, float& ga, float& gb) {
-        if constexpr (OP == VC_ADD) { ga = gv; gb = gv; }
-        else if constexpr (OP == VC_SUB) { ga = gv; gb = -gv; }
-        else if constexpr (OP == VC_MUL) { ga = vjp<V_MUL>(gv, bv, 0.f); gb = vjp<V_MUL>(gv, av, 0.f); }
-        else { ga = vjp<V_DIV_A>(gv, bv, 0.f); gb = vjp<V_DIV_B>(gv, av, bv); }
-    };
-    constexpr bool NEED_A = OP == VC_MUL || OP == VC_DIV;
-    constexpr bool NEED_B = OP == VC_MUL || OP == VC_DIV;
+    constexpr bool NEED_AB = OP == VC_MUL || OP == VC_DIV;
     if constexpr (VEC) {
         const std::size_t n4 = n >> 2;
-        for (std::size_t i = tid; i < n4; i += stride) {
+        std::size_t i = tid;
+        for (; i + stride < n4; i += 2 * stride) {
+            const std::size_t k0 = i * 4, k1 = (i + stride) * 4;
+            const float4 g0 = ld4_stream(g + k0), g1 = ld4_stream(g + k1);
+            const float4 a0 = NEED_AB ? ld4_stream(a + k0) : g0, a1 = NEED_AB ? ld4_stream(a + k1) : g1;
+            const float4 b0 = NEED_AB ? ld4_stream(b + k0) : g0, b1 = NEED_AB ? ld4_stream(b + k1) : g1;
+            float4 ga0, gb0, ga1, gb1;
+            bb_four<OP>(a0, b0, g0, ga0, gb0);
+            bb_four<OP>(a1, b1, g1, ga1, gb1);
+            st4_stream(da + k0, ga0);
+            st4_stream(db + k0, gb0);
+            st4_stream(da + k1, ga1);
+            st4_stream(db + k1, gb1);
+        }
+        for (; i < n4; i += stride) {
             const std::size_t k = i * 4;
             const float4 gv = ld4_stream(g + k);
-            const float4 av = NEED_A ? ld4_stream(a + k) : gv;
-            const float4 bv = NEED_B ? ld4_stream(b + k) : gv;
+            const float4 av = NEED_AB ? ld4_stream(a + k) : gv;
+            const float4 bv = NEED_AB ? ld4_stream(b + k) : gv;
             float4 ga, gb;
-            one(av.x, bv.x, gv.x, ga.x, gb.x);
-            one(av.y, bv.y, gv.y, ga.y, gb.y);
-            one(av.z, bv.z, gv.z, ga.z, gb.z);
-            one(av.w, bv.w, gv.w, ga.w, gb.w);
+            bb_four<OP>(av, bv, gv, ga, gb);
             st4_stream(da + k, ga);
             st4_stream(db + k, gb);
         }
-        for (std::size_t k = n4 * 4 + tid; k < n; k += stride) one(NEED_A ? a[k] : 0.f, NEED_B ? b[k] : 0.f, g[k], da[k], db[k]);
+        for (std::size_t k = n4 * 4 + tid; k < n; k += stride)
+            bb_one<OP>(NEED_AB ? a[k] : 0.f, NEED_AB ? b[k] : 0.f, g[k], da[k], db[k]);
     } else {
-        for (std::size_t k = tid; k < n; k += stride) one(NEED_A ? a[k] : 0.f, NEED_B ? b[k] : 0.f, g[k], da[k], db[k]);
+        for (std::size_t k = tid; k < n; k += stride)
+            bb_one<OP>(NEED_AB ? a[k] : 0.f, NEED_AB ? b[k] : 0.f, g[k], da[k], db[k]);
     }
 }
 
@@ -486,13 +603,20 @@ max_row_kernel(const float* __restrict__ in, unsigned long long outer, unsigned 
         const float* x = in + row * length;
         MaxCand c{0.0f, -1};
         if constexpr (VEC) {
-            for (unsigned long long e = e0 + threadIdx.x * 4; e < e1; e += kThreads * 4) {
-                const float4 v = ldg4(x + e);
+            constexpr unsigned long long STEP = kThreads * 4ull;
+            auto take4 = [&](const float4& v, unsigned long long e) {
                 c = max_take(c, v.x, static_cast<long long>(e));
                 c = max_take(c, v.y, static_cast<long long>(e + 1));
                 c = max_take(c, v.z, static_cast<long long>(e + 2));
                 c = max_take(c, v.w, static_cast<long long>(e + 3));
+            };
+            unsigned long long e = e0 + threadIdx.x * 4;
+            for (; e + STEP < e1; e += 2 * STEP) {  // two loads in flight, taken in index order
+                const float4 v0 = ldg4(x + e), v1 = ldg4(x + e + STEP);
+                take4(v0, e);
+                take4(v1, e + STEP);
             }
+            for (; e < e1; e += STEP) take4(ldg4(x + e), e);
         } else {
             for (unsigned long long e = e0 + threadIdx.x; e < e1; e += kThreads)
                 c = max_take(c, __ldg(x + e), static_cast<long long>(e));
@@ -518,22 +642,52 @@ max_row_finish(const float* __restrict__ in, unsigned long long outer, unsigned 
     }
 }
 
-// COLUMN (inner > 1): grid = (ceil(inner/256), min(outer, 65535), segments).
+// COLUMN (inner > 1): grid = (ceil(inner/(256*V)), min(outer, 65535), segments).
+// VEC: each thread owns 4 adjacent columns (float4 loads); four positions of
+// the reduced axis in flight, taken in index order.
+template <bool VEC>
 __global__ void __launch_bounds__(kThreads)
 max_col_kernel(const float* __restrict__ in, unsigned long long outer, unsigned long long length,
                unsigned long long inner, unsigned long long seg, unsigned S, MaxOut o,
                float* __restrict__ pv, long long* __restrict__ pi) {
-    const unsigned long long i = static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    constexpr int V = VEC ? 4 : 1;
+    const unsigned long long i = (static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x) * V;
     if (i >= inner) return;
     const unsigned s = blockIdx.z;
     const unsigned long long a0 = s * seg, a1 = min(length, a0 + seg);
     for (unsigned long long ob = blockIdx.y; ob < outer; ob += gridDim.y) {
         const float* x = in + ob * length * inner + i;
-        MaxCand c{0.0f, -1};
-        for (unsigned long long a = a0; a < a1; ++a) c = max_take(c, __ldg(x + a * inner), static_cast<long long>(a));
-        const unsigned long long k = ob * inner + i;
-        if (S == 1) max_finish_write(c, __ldg(x), o, k);
-        else { pv[s * outer * inner + k] = c.v; pi[s * outer * inner + k] = c.i; }
+        MaxCand c[V];
+#pragma unroll
+        for (int v = 0; v < V; ++v) c[v] = MaxCand{0.0f, -1};
+        auto take = [&](const float4& v, unsigned long long a) {
+            const long long ai = static_cast<long long>(a);
+            c[0] = max_take(c[0], v.x, ai);
+            if constexpr (VEC) {
+                c[1] = max_take(c[1], v.y, ai);
+                c[2] = max_take(c[2], v.z, ai);
+                c[3] = max_take(c[3], v.w, ai);
+            }
+        };
+        auto load = [&](unsigned long long a) -> float4 {
+            if constexpr (VEC) return ldg4(x + a * inner);
+            else return make_float4(__ldg(x + a * inner), 0.f, 0.f, 0.f);
+        };
+        unsigned long long a = a0;
+        for (; a + 3 < a1; a += 4) {
+            const float4 v0 = load(a), v1 = load(a + 1), v2 = load(a + 2), v3 = load(a + 3);
+            take(v0, a);
+            take(v1, a + 1);
+            take(v2, a + 2);
+            take(v3, a + 3);
+        }
+        for (; a < a1; ++a) take(load(a), a);
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+            const unsigned long long k = ob * inner + i + v;
+            if (S == 1) max_finish_write(c[v], __ldg(x + v), o, k);
+            else { pv[s * outer * inner + k] = c[v].v; pi[s * outer * inner + k] = c[v].i; }
+        }
     }
 }
 
@@ -557,8 +711,7 @@ static void launch_max(const float* in, std::size_t outer, std::size_t length, s
     if (length == 0) fail(VC_ERR_INVALID, "max/argmax over an empty axis is undefined");
     cudaStream_t st = stream();
     if (inner == 1) {
-        unsigned long long S = std::max<unsigned long long>(1, (length + kRowChunk - 1) / kRowChunk);
-        S = std::min<unsigned long long>(S, 65535);
+        const unsigned long long S = row_segments(outer, length);
         unsigned long long seg = ((length + S - 1) / S + 3) / 4 * 4;
         const unsigned Sn = static_cast<unsigned>((length + seg - 1) / seg);
         const bool vec = aligned16(in) && length % 4 == 0;
@@ -573,7 +726,8 @@ static void launch_max(const float* in, std::size_t outer, std::size_t length, s
         }
         return;
     }
-    const unsigned long long lanes = inner;
+    const bool vec = inner % 4 == 0 && aligned16(in);
+    const unsigned long long lanes = vec ? inner / 4 : inner;
     const unsigned long long threads_now = lanes * outer;
     unsigned long long S = (kTargetThreads + threads_now - 1) / threads_now;
     S = std::min<unsigned long long>(S, (length + kMinSegment - 1) / kMinSegment);
@@ -581,9 +735,10 @@ static void launch_max(const float* in, std::size_t outer, std::size_t length, s
     const unsigned long long seg = (length + S - 1) / S;
     const unsigned Sn = static_cast<unsigned>((length + seg - 1) / seg);
     Scratch pv(Sn > 1 ? outer * inner * Sn * sizeof(float) : 8), pi(Sn > 1 ? outer * inner * Sn * sizeof(long long) : 8);
-    dim3 grid(static_cast<unsigned>((inner + kThreads - 1) / kThreads),
+    dim3 grid(static_cast<unsigned>((lanes + kThreads - 1) / kThreads),
               static_cast<unsigned>(std::min<std::size_t>(outer, 65535)), Sn);
-    max_col_kernel<<<grid, kThreads, 0, st>>>(in, outer, length, inner, seg, Sn, o, pv.as<float>(), pi.as<long long>());
+    if (vec) max_col_kernel<true><<<grid, kThreads, 0, st>>>(in, outer, length, inner, seg, Sn, o, pv.as<float>(), pi.as<long long>());
+    else max_col_kernel<false><<<grid, kThreads, 0, st>>>(in, outer, length, inner, seg, Sn, o, pv.as<float>(), pi.as<long long>());
     check_launch("max_col");
     if (Sn > 1) {
         max_col_finish<<<grid_for(outer * inner, kThreads), kThreads, 0, st>>>(in, outer, length, inner, Sn, pv.as<float>(), pi.as<long long>(), o);

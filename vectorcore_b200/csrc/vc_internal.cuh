@@ -116,17 +116,11 @@ struct FastDiv {
 __device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
 __device__ __forceinline__ void st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
 
-// Streaming (evict-first) variants for data touched once.
-__device__ __forceinline__ float4 ld4_stream(const float* p) {
-    float4 v;
-    asm volatile("ld.global.cs.v4.f32 {%0,%1,%2,%3}, [%4];"
-                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
-    return v;
-}
-__device__ __forceinline__ void st4_stream(float* p, float4 v) {
-    asm volatile("st.global.cs.v4.f32 [%0], {%1,%2,%3,%4};"
-                 :: "l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w) : "memory");
-}
+// Streaming (evict-first, ld/st.global.cs) variants for data touched once.
+// Intrinsics rather than volatile asm so the compiler may hoist the loads of
+// later iterations above earlier stores.
+__device__ __forceinline__ float4 ld4_stream(const float* p) { return __ldcs(reinterpret_cast<const float4*>(p)); }
+__device__ __forceinline__ void st4_stream(float* p, float4 v) { __stcs(reinterpret_cast<float4*>(p), v); }
 
 // Max/argmax candidate under the reference's scan semantics: a larger value
 // wins; equal values (==, so -0 == +0) keep the smaller index; NaN is never
@@ -207,5 +201,9 @@ struct ShapeView {
 
 std::size_t checked_numel(const size_t* shape, int rank);
 void validate_rank(int rank, const char* what);
+
+// out (out_shape) = src broadcast from src_shape, bit for bit (elementwise.cu).
+void broadcast_copy(const float* src, const size_t* src_shape, int src_rank, float* out,
+                    const size_t* out_shape, int out_rank);
 
 }  // namespace vc
