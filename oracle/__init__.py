@@ -384,6 +384,8 @@ def build(quiet: bool = True) -> None:
     import subprocess
 
     ref = os.environ.get("VECTORCORE_REF", "/root/reference")
-    targets = ["oracle"] + (["ref"] if Path(ref, "src").is_dir() else [])
+    # "slot" links the reference's sources to the CUDA library, so it needs
+    # vectorcore_b200/_lib/libvc_cuda.so to be built first.
+    targets = ["oracle"] + (["ref", "slot"] if Path(ref, "src").is_dir() else [])
     subprocess.run(["make", "-s", "-C", str(HERE), f"REF={ref}", *targets], check=True,
                    stdout=subprocess.DEVNULL if quiet else None)

@@ -296,16 +296,20 @@ reduce_row_kernel(const float* __restrict__ g, const float* __restrict__ p, cons
     }
 }
 
-// Combine ROW partials [K][S] in segment order.
+// Combine ROW partials [K][S]: one CTA per output, thread t adds partials
+// t, t+256, ... and a fixed block tree combines the threads (an order that
+// depends only on S), so few outputs with many segments (a full sum) finish in
+// parallel rather than in one thread.
 __global__ void __launch_bounds__(kThreads)
 reduce_row_finish(const double* __restrict__ partial, unsigned S, unsigned long long K, float divisor,
                   float* __restrict__ out) {
-    const unsigned long long stride = static_cast<unsigned long long>(gridDim.x) * blockDim.x;
-    for (unsigned long long k = static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x; k < K;
-         k += stride) {
+    __shared__ double s_red[32];
+    for (unsigned long long k = blockIdx.x; k < K; k += gridDim.x) {
         double acc = 0.0;
-        for (unsigned s = 0; s < S; ++s) acc += partial[k * S + s];
-        out[k] = round_out(acc, divisor);
+        for (unsigned s = threadIdx.x; s < S; s += blockDim.x) acc += partial[k * S + s];
+        acc = block_sum(acc, s_red);
+        if (threadIdx.x == 0) out[k] = round_out(acc, divisor);
+        __syncthreads();
     }
 }
 
@@ -488,7 +492,8 @@ static void launch_vjp_reduce(const Src ops[3], const size_t* src_shape, int src
 #undef VC_ROW
     check_launch("reduce_row");
     if (d.S > 1) {
-        reduce_row_finish<<<grid_for(d.K, kThreads), kThreads, 0, stream()>>>(partial.as<double>(), d.S, d.K, divisor, out);
+        reduce_row_finish<<<static_cast<unsigned>(std::min<unsigned long long>(d.K, static_cast<unsigned long long>(sm_count()) * 8)),
+                            kThreads, 0, stream()>>>(partial.as<double>(), d.S, d.K, divisor, out);
         check_launch("reduce_row_finish");
     }
 }
@@ -633,12 +638,17 @@ max_row_kernel(const float* __restrict__ in, unsigned long long outer, unsigned 
 __global__ void __launch_bounds__(kThreads)
 max_row_finish(const float* __restrict__ in, unsigned long long outer, unsigned long long length, unsigned S,
                const float* __restrict__ pv, const long long* __restrict__ pi, MaxOut o) {
-    const unsigned long long stride = static_cast<unsigned long long>(gridDim.x) * blockDim.x;
-    for (unsigned long long row = static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x; row < outer;
-         row += stride) {
+    // One CTA per row. max_combine (larger value, then smaller index) is
+    // associative and commutative, so the tree order cannot change the result.
+    __shared__ float s_v[32];
+    __shared__ long long s_i[32];
+    for (unsigned long long row = blockIdx.x; row < outer; row += gridDim.x) {
         MaxCand c{0.0f, -1};
-        for (unsigned s = 0; s < S; ++s) c = max_combine(c, MaxCand{pv[row * S + s], pi[row * S + s]});
-        max_finish_write(c, in[row * length], o, row);
+        for (unsigned s = threadIdx.x; s < S; s += blockDim.x)
+            c = max_combine(c, MaxCand{pv[row * S + s], pi[row * S + s]});
+        c = block_max(c, s_v, s_i);
+        if (threadIdx.x == 0) max_finish_write(c, in[row * length], o, row);
+        __syncthreads();
     }
 }
 
@@ -721,7 +731,8 @@ static void launch_max(const float* in, std::size_t outer, std::size_t length, s
         else max_row_kernel<false><<<grid, kThreads, 0, st>>>(in, outer, length, seg, Sn, o, pv.as<float>(), pi.as<long long>());
         check_launch("max_row");
         if (Sn > 1) {
-            max_row_finish<<<grid_for(outer, kThreads), kThreads, 0, st>>>(in, outer, length, Sn, pv.as<float>(), pi.as<long long>(), o);
+            max_row_finish<<<static_cast<unsigned>(std::min<std::size_t>(outer, static_cast<std::size_t>(sm_count()) * 8)),
+                             kThreads, 0, st>>>(in, outer, length, Sn, pv.as<float>(), pi.as<long long>(), o);
             check_launch("max_row_finish");
         }
         return;
