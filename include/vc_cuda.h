@@ -282,6 +282,26 @@ vc_status vc_cuda_matmul(const float* a, const float* b, float* out, size_t m, s
  * Replaces MetalBackend::transpose_last2 (metal_backend.hpp:38-39). */
 vc_status vc_cuda_transpose_last2(const float* in, float* out, size_t batch, size_t rows, size_t cols);
 
+/* ---- allocation-free sum ---------------------------------------------------- */
+
+/* out[0] = sum of the `count` floats at `in` (device memory), the same value
+ * vc_cuda_reduce_all(VC_REDUCE_SUM, ...) computes (double accumulation, one
+ * rounding), for callers that must not allocate device memory: hosts that
+ * reserved the device's memory up front under a hard budget, or loops that
+ * cannot stall on cudaMalloc / cudaFree. No counterpart in the reference.
+ *  - Allocates nothing: its scratch (4096 doubles, 32 KiB) is an array
+ *    compiled into this library, held by every GPU that loads it until the
+ *    process exits. Call vc_cuda_init first (it creates the stream).
+ *  - count <= 268435456 (2^28, one partial per 65536 elements); larger
+ *    counts fail with VC_ERR_OVERFLOW before anything is launched.
+ *  - The first call on a device looks up the array's device address
+ *    (cudaGetSymbolAddress, which may load this library's kernels onto the
+ *    device); make that first call before any stream capture.
+ *  - Every call uses the same array: calls that overlap on the GPU (other
+ *    streams, other host threads with their own streams) race. Calls on the
+ *    library's one stream are ordered and safe. */
+vc_status vc_cuda_reduce_sum_noalloc(const float* in, size_t count, float* out);
+
 #ifdef __cplusplus
 }
 #endif

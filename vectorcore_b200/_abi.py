@@ -101,6 +101,7 @@ _SIGS = {
     "vc_cuda_cross_entropy_backward": (c_int, [_f, c_void_p, _f, _f, _f, c_size_t, c_size_t, c_size_t, _f]),
     "vc_cuda_matmul": (c_int, [_f, _f, _f, c_size_t, c_size_t, c_size_t, _szp, _szp, c_size_t, c_int, c_int]),
     "vc_cuda_transpose_last2": (c_int, [_f, _f, c_size_t, c_size_t, c_size_t]),
+    "vc_cuda_reduce_sum_noalloc": (c_int, [_f, c_size_t, _f]),
 }
 
 
