@@ -342,9 +342,12 @@ def run_ours(args):
 
         import torch.distributed as dist
 
+        # The sweep has no data-path collective (each rank owns a row shard);
+        # the process group only carries the barrier and the max-over-ranks of
+        # the timings, on the host after a CUDA synchronise, so gloo suffices
+        # (and keeps NCCL's banner off stdout).
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
     _abi.check(_abi.lib.vc_cuda_init(local))
     torch.cuda.set_device(local)
     be = B.CudaBackend.instance()
@@ -357,6 +360,11 @@ def run_ours(args):
 
     def step(events=None):
         outs = []
+        if events is not None:
+            # Keep the GPU busy for ~50 us while the host queues the step, so
+            # the first op's events do not include host launch latency.
+            with torch.cuda.stream(vstream):
+                torch.cuda._sleep(100_000)
         for i, (_, _, fn) in enumerate(ops):
             if events is not None:
                 events[i][0].record(vstream)
@@ -390,7 +398,7 @@ def run_ours(args):
     total_ms = start.elapsed_time(stop)
     gpu_launches = ctx.launches
     step_ms_local = sum(per_op_ms) / args.steps  # device time of the ops (no host readback gaps)
-    t = torch.tensor([step_ms_local], device=f"cuda:{local}", dtype=torch.float64)
+    t = torch.tensor([step_ms_local], dtype=torch.float64)  # host tensor: gloo
     if dist is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     step_ms = float(t.item())
@@ -482,7 +490,7 @@ def measure_e2e(args, wl, step, barrier, _abi, dist, torch, local, bytes_per_ste
     barrier()
     secs = (time.perf_counter() - t0) / steps
     if dist is not None:
-        te = torch.tensor([secs], device=f"cuda:{local}", dtype=torch.float64)
+        te = torch.tensor([secs], dtype=torch.float64)
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
         secs = float(te.item())
     for p, _ in hosts.values():

@@ -268,6 +268,55 @@ vc_status vc_cuda_cross_entropy_backward(const float* logits, const int64_t* tar
                                          const float* upstream, size_t batch, size_t classes,
                                          size_t batch_total, float* dlogits);
 
+/* ---- multi-GPU: leading-axis shards, partials combined in rank order -----
+ * No counterpart in the reference (it is single-device). One process per
+ * GPU; each rank reduces its shard into an unrounded partial, the partials
+ * are all-gathered ([nranks][count], rank-major), and every rank combines
+ * them in rank order 0..R-1, so results are independent of the collective's
+ * internal order. */
+
+/* This shard's part of a reduction over the middle axis of [outer, length,
+ * inner]: SUM/MEAN -> partial_sum (double, not rounded); MAX/ARGMAX ->
+ * partial_value + partial_index (int64, with index_base -- the shard's first
+ * row -- added). continuation != 0 for every shard but the first: the
+ * "NaN at index 0 wins" rule belongs to the first shard, and a later shard
+ * without a candidate reports index -1. */
+vc_status vc_cuda_reduce_axis_partial(int op, const float* in, size_t outer, size_t length, size_t inner,
+                                      int64_t index_base, int continuation, double* partial_sum,
+                                      float* partial_value, int64_t* partial_index);
+
+/* vc_cuda_binary_backward's reductions, written as unrounded double
+ * partials (e.g. a bias gradient over a sharded batch axis). */
+vc_status vc_cuda_binary_backward_partial(int op,
+                                          const float* a, const size_t* a_shape, int a_rank,
+                                          const float* b, const size_t* b_shape, int b_rank,
+                                          const float* g, const size_t* g_shape, int g_rank,
+                                          double* da_partial, double* db_partial);
+
+/* Combine nranks partials in rank order. SUM/MEAN: out = float(sum) (negated
+ * when negate != 0), divided by divisor when divisor != 0 -- the mean
+ * cross-entropy of a sharded batch is (SUM, negate=1, divisor=B).
+ * MAX/ARGMAX: the first maximal element (a lower rank wins ties); out_value
+ * gets the value (MAX) or the index as float (ARGMAX), out_index the int64. */
+vc_status vc_cuda_combine_partials(int op, const double* partial_sum, const float* partial_value,
+                                   const int64_t* partial_index, int nranks, size_t count, float divisor,
+                                   int negate, float* out_value, int64_t* out_index);
+
+/* NCCL communicator (libnccl.so.2 loaded at run time). Rank 0 creates the
+ * 128-byte id and every rank passes it to comm_init (the id travels through
+ * any host channel, e.g. torch.distributed's store). Non-blocking; each wait
+ * is bounded by timeout_ms, after which the communicator is aborted and the
+ * call returns VC_ERR_TIMEOUT. */
+vc_status vc_cuda_comm_unique_id(void* id, size_t bytes);
+vc_status vc_cuda_comm_init(int nranks, int rank, const void* id, size_t bytes, int timeout_ms);
+/* recv [nranks * bytes_per_rank] = every rank's send, in rank order; enqueued. */
+vc_status vc_cuda_comm_allgather(const void* send, void* recv, size_t bytes_per_rank);
+/* Wait for the stream with a deadline, watching the communicator for errors. */
+vc_status vc_cuda_comm_synchronize(int timeout_ms);
+vc_status vc_cuda_comm_destroy(void);
+int vc_cuda_comm_size(void);
+int vc_cuda_comm_rank(void);
+
 /* ---- existing ops (correct, not tuned: off the bandwidth-bound path) ---- */
 
 /* Batched out[z] (m x n) = op(A)[a_offsets[z]..] @ op(B)[b_offsets[z]..];

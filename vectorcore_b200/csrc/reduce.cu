@@ -26,9 +26,9 @@ namespace {
 constexpr unsigned kThreads = 256;
 // Aim for about this many threads of work before splitting a reduction into
 // segments (a constant, so the split depends on the problem size alone).
-constexpr unsigned long long kTargetThreads = 1ull << 18;
+constexpr unsigned long long kTargetThreads = 1ull << 19;
 constexpr unsigned long long kMinSegment = 16;         // reduced positions per segment (column)
-constexpr unsigned long long kRowTargetCtas = 1024;    // aim for this many (row, segment) CTAs
+constexpr unsigned long long kRowTargetCtas = 4096;    // aim for this many (row, segment) CTAs
 constexpr unsigned long long kRowMinSegment = 4096;    // elements per row segment, at least
 
 // Segments per row for a ROW-layout reduction of K rows of W elements: enough
@@ -79,6 +79,8 @@ struct RedDesc {
     unsigned long long seg; // COLUMN: reduced positions per segment; ROW: elements per segment
     unsigned S;             // segments
     float divisor;          // mean: divide the rounded sum by this (0 = none)
+    double* out_d;          // when set: write the unrounded double sums here
+                            // (a shard's partial for a cross-GPU combine)
 };
 
 __device__ __forceinline__ void decode(unsigned long long idx, int n, const unsigned long long* dims,
@@ -190,7 +192,10 @@ reduce_col_kernel(const float* __restrict__ g, const float* __restrict__ p, cons
             advance();
         }
         const unsigned long long o = ko * d.inner + i0;
-        if (d.S == 1) {
+        if (d.S == 1 && d.out_d) {
+#pragma unroll
+            for (int v = 0; v < V; ++v) d.out_d[o + v] = acc[v];
+        } else if (d.S == 1) {
             if constexpr (VEC)
                 st4(out + o, make_float4(round_out(acc[0], d.divisor), round_out(acc[1], d.divisor),
                                          round_out(acc[2], d.divisor), round_out(acc[3], d.divisor)));
@@ -206,13 +211,14 @@ reduce_col_kernel(const float* __restrict__ g, const float* __restrict__ p, cons
 // Combine COLUMN partials [S][K*inner] in segment order.
 __global__ void __launch_bounds__(kThreads)
 reduce_col_finish(const double* __restrict__ partial, unsigned S, unsigned long long count,
-                  float divisor, float* __restrict__ out) {
+                  float divisor, float* __restrict__ out, double* __restrict__ out_d) {
     const unsigned long long stride = static_cast<unsigned long long>(gridDim.x) * blockDim.x;
     for (unsigned long long o = static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x; o < count;
          o += stride) {
         double acc = 0.0;
         for (unsigned s = 0; s < S; ++s) acc += partial[static_cast<unsigned long long>(s) * count + o];
-        out[o] = round_out(acc, divisor);
+        if (out_d) out_d[o] = acc;
+        else out[o] = round_out(acc, divisor);
     }
 }
 
@@ -275,21 +281,20 @@ reduce_row_kernel(const float* __restrict__ g, const float* __restrict__ p, cons
         decode(k, d.nk, d.kdims, d.ks, base, nullptr);
         double acc0 = 0.0, acc1 = 0.0;
         unsigned long long e = e0 + threadIdx.x * V;
-        // four independent groups in flight per thread
-        for (; e + 3 * STEP < e1; e += 4 * STEP) {
-            const float4 v0 = row_fetch<F, VEC, HAS_R>(g, p, q, d, base, e);
-            const float4 v1 = row_fetch<F, VEC, HAS_R>(g, p, q, d, base, e + STEP);
-            const float4 v2 = row_fetch<F, VEC, HAS_R>(g, p, q, d, base, e + 2 * STEP);
-            const float4 v3 = row_fetch<F, VEC, HAS_R>(g, p, q, d, base, e + 3 * STEP);
-            row_accumulate<VEC>(acc0, acc1, v0);
-            row_accumulate<VEC>(acc0, acc1, v1);
-            row_accumulate<VEC>(acc0, acc1, v2);
-            row_accumulate<VEC>(acc0, acc1, v3);
+        // eight independent groups in flight per thread (the bytes in flight,
+        // not the arithmetic, set the pace of a streaming reduction)
+        for (; e + 7 * STEP < e1; e += 8 * STEP) {
+            float4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = row_fetch<F, VEC, HAS_R>(g, p, q, d, base, e + u * STEP);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) row_accumulate<VEC>(acc0, acc1, v[u]);
         }
         for (; e < e1; e += STEP) row_accumulate<VEC>(acc0, acc1, row_fetch<F, VEC, HAS_R>(g, p, q, d, base, e));
         const double total = block_sum(acc0 + acc1, s_red);
         if (threadIdx.x == 0) {
-            if (d.S == 1) out[k] = round_out(total, d.divisor);
+            if (d.S == 1 && d.out_d) d.out_d[k] = total;
+            else if (d.S == 1) out[k] = round_out(total, d.divisor);
             else partial[k * d.S + s] = total;
         }
         __syncthreads();
@@ -302,13 +307,16 @@ reduce_row_kernel(const float* __restrict__ g, const float* __restrict__ p, cons
 // parallel rather than in one thread.
 __global__ void __launch_bounds__(kThreads)
 reduce_row_finish(const double* __restrict__ partial, unsigned S, unsigned long long K, float divisor,
-                  float* __restrict__ out) {
+                  float* __restrict__ out, double* __restrict__ out_d) {
     __shared__ double s_red[32];
     for (unsigned long long k = blockIdx.x; k < K; k += gridDim.x) {
         double acc = 0.0;
         for (unsigned s = threadIdx.x; s < S; s += blockDim.x) acc += partial[k * S + s];
         acc = block_sum(acc, s_red);
-        if (threadIdx.x == 0) out[k] = round_out(acc, divisor);
+        if (threadIdx.x == 0) {
+            if (out_d) out_d[k] = acc;
+            else out[k] = round_out(acc, divisor);
+        }
         __syncthreads();
     }
 }
@@ -340,7 +348,7 @@ static Src align(const float* ptr, const size_t* shape, int rank, const size_t* 
 
 template <int F>
 static void launch_vjp_reduce(const Src ops[3], const size_t* src_shape, int src_rank, const size_t* t_shape,
-                              int t_rank, float* out, float divisor) {
+                              int t_rank, float* out, float divisor, double* out_d = nullptr) {
     // 1. classify source dims: 0 drop (size 1), 1 kept, 2 reduced.
     if (t_rank > src_rank) fail(VC_ERR_INVALID, "sum_to_shape: cannot reduce to a larger rank");
     const int lead = src_rank - t_rank;
@@ -358,7 +366,7 @@ static void launch_vjp_reduce(const Src ops[3], const size_t* src_shape, int src
     // and broadcast the result (e.g. the gradient of a * b for the scalar
     // upstream of sum(): 2^32 products collapse to 2^17). Same values,
     // bit for bit: each output sums the same products in the same order.
-    if (outsz > 0) {
+    if (outsz > 0 && !out_d) {
         bool any = false;
         size_t c_src[kMaxRank], c_tgt[kMaxRank], full_tgt[kMaxRank];
         for (int i = 0; i < src_rank; ++i) {
@@ -401,6 +409,7 @@ static void launch_vjp_reduce(const Src ops[3], const size_t* src_shape, int src
     if (outsz == 0) return;
     RedDesc d{};
     d.divisor = divisor;
+    d.out_d = out_d;
     if (nd == 0 || dims[nd - 1].cls == 1) {
         // COLUMN (also covers "nothing to reduce").
         const unsigned long long inner = nd ? dims[nd - 1].size : 1;
@@ -446,7 +455,7 @@ static void launch_vjp_reduce(const Src ops[3], const size_t* src_shape, int src
         check_launch("reduce_col");
         if (d.S > 1) {
             const unsigned long long count = d.K * d.inner;
-            reduce_col_finish<<<grid_for(count, kThreads), kThreads, 0, stream()>>>(partial.as<double>(), d.S, count, divisor, out);
+            reduce_col_finish<<<grid_for(count, kThreads), kThreads, 0, stream()>>>(partial.as<double>(), d.S, count, divisor, out, out_d);
             check_launch("reduce_col_finish");
         }
         return;
@@ -493,19 +502,19 @@ static void launch_vjp_reduce(const Src ops[3], const size_t* src_shape, int src
     check_launch("reduce_row");
     if (d.S > 1) {
         reduce_row_finish<<<static_cast<unsigned>(std::min<unsigned long long>(d.K, static_cast<unsigned long long>(sm_count()) * 8)),
-                            kThreads, 0, stream()>>>(partial.as<double>(), d.S, d.K, divisor, out);
+                            kThreads, 0, stream()>>>(partial.as<double>(), d.S, d.K, divisor, out, out_d);
         check_launch("reduce_row_finish");
     }
 }
 
 static void vjp_reduce(int f, const Src ops[3], const size_t* src_shape, int src_rank, const size_t* t_shape,
-                       int t_rank, float* out, float divisor = 0.0f) {
+                       int t_rank, float* out, float divisor = 0.0f, double* out_d = nullptr) {
     switch (f) {
-        case V_G: return launch_vjp_reduce<V_G>(ops, src_shape, src_rank, t_shape, t_rank, out, divisor);
-        case V_NEG: return launch_vjp_reduce<V_NEG>(ops, src_shape, src_rank, t_shape, t_rank, out, divisor);
-        case V_MUL: return launch_vjp_reduce<V_MUL>(ops, src_shape, src_rank, t_shape, t_rank, out, divisor);
-        case V_DIV_A: return launch_vjp_reduce<V_DIV_A>(ops, src_shape, src_rank, t_shape, t_rank, out, divisor);
-        default: return launch_vjp_reduce<V_DIV_B>(ops, src_shape, src_rank, t_shape, t_rank, out, divisor);
+        case V_G: return launch_vjp_reduce<V_G>(ops, src_shape, src_rank, t_shape, t_rank, out, divisor, out_d);
+        case V_NEG: return launch_vjp_reduce<V_NEG>(ops, src_shape, src_rank, t_shape, t_rank, out, divisor, out_d);
+        case V_MUL: return launch_vjp_reduce<V_MUL>(ops, src_shape, src_rank, t_shape, t_rank, out, divisor, out_d);
+        case V_DIV_A: return launch_vjp_reduce<V_DIV_A>(ops, src_shape, src_rank, t_shape, t_rank, out, divisor, out_d);
+        default: return launch_vjp_reduce<V_DIV_B>(ops, src_shape, src_rank, t_shape, t_rank, out, divisor, out_d);
     }
 }
 
@@ -863,6 +872,45 @@ static void launch_axis_expand(int mode, const float* g, const long long* idx, c
     else launch_expand_mode<2>(g, idx, idxf, out, outer, length, inner);
 }
 
+// ---------------------------------------------------------------------------
+// Cross-GPU combine of shard partials laid out [nranks][count] (the order of
+// an all-gather), always in rank order 0..R-1 -- independent of the order in
+// which the collective moved the bytes.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads)
+combine_sum_kernel(const double* __restrict__ parts, int nranks, unsigned long long count, float divisor, int negate,
+                   float* __restrict__ out) {
+    const unsigned long long stride = static_cast<unsigned long long>(gridDim.x) * blockDim.x;
+    for (unsigned long long k = static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x; k < count;
+         k += stride) {
+        double acc = 0.0;
+        for (int r = 0; r < nranks; ++r) acc += parts[static_cast<unsigned long long>(r) * count + k];
+        float s = static_cast<float>(acc);
+        if (negate) s = -s;
+        out[k] = divisor != 0.0f ? s / divisor : s;
+    }
+}
+
+// Rank 0's partial already carries the "NaN at index 0" rule; later shards
+// report -1 when they have no candidate. max_combine keeps the smaller
+// (global) index on ties, i.e. the lower rank.
+__global__ void __launch_bounds__(kThreads)
+combine_max_kernel(const float* __restrict__ vals, const long long* __restrict__ idx, int nranks,
+                   unsigned long long count, int argmax_as_value, float* __restrict__ out_value,
+                   long long* __restrict__ out_index) {
+    const unsigned long long stride = static_cast<unsigned long long>(gridDim.x) * blockDim.x;
+    for (unsigned long long k = static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x; k < count;
+         k += stride) {
+        MaxCand c{0.0f, -1};
+        for (int r = 0; r < nranks; ++r) {
+            const unsigned long long o = static_cast<unsigned long long>(r) * count + k;
+            c = max_combine(c, MaxCand{vals[o], idx[o]});
+        }
+        if (out_value) out_value[k] = argmax_as_value ? static_cast<float>(c.i) : c.v;
+        if (out_index) out_index[k] = c.i;
+    }
+}
+
 }  // namespace
 
 }  // namespace vc
@@ -1029,6 +1077,111 @@ vc_status vc_cuda_reduce_axis_backward(int op, const float* g, const int64_t* in
         default: fail(VC_ERR_INVALID, "reduce_axis_backward: operation has no backward rule");
     }
     launch_axis_expand(mode, g, reinterpret_cast<const long long*>(indices), nullptr, out, outer, length, inner);
+    VC_API_END
+}
+
+}  // extern "C"
+
+// ---- multi-GPU: shard partials and their rank-order combine ------------------
+
+extern "C" {
+
+vc_status vc_cuda_reduce_axis_partial(int op, const float* in, size_t outer, size_t length, size_t inner,
+                                      int64_t index_base, int continuation, double* partial_sum,
+                                      float* partial_value, int64_t* partial_index) {
+    VC_API_BEGIN
+    ensure_init();
+    const size_t dims[3] = {outer, length, inner};
+    checked_numel(dims, 3);
+    const std::size_t count = outer * inner;
+    if (!count) return VC_OK;
+    if (op == VC_REDUCE_SUM || op == VC_REDUCE_MEAN) {
+        if (!partial_sum) fail(VC_ERR_INVALID, "reduce_axis_partial: null partial_sum");
+        if (length == 0) {
+            VC_CUDA(cudaMemsetAsync(partial_sum, 0, count * sizeof(double), stream()));
+            return VC_OK;
+        }
+        Src ops[3];
+        const size_t target[3] = {outer, 1, inner};
+        ops[0] = align(in, dims, 3, dims, 3, "reduce_axis_partial");
+        vjp_reduce(V_G, ops, dims, 3, target, 3, nullptr, 0.0f, partial_sum);
+        return VC_OK;
+    }
+    if (op != VC_REDUCE_MAX && op != VC_REDUCE_ARGMAX) fail(VC_ERR_INVALID, "unknown reduction");
+    if (!partial_value || !partial_index) fail(VC_ERR_INVALID, "reduce_axis_partial: null partial_value/index");
+    if (length == 0) {
+        if (!continuation) fail(VC_ERR_INVALID, "max/argmax over an empty axis is undefined");
+        // an empty later shard has no candidate: value 0, index -1
+        VC_CUDA(cudaMemsetAsync(partial_value, 0, count * sizeof(float), stream()));
+        VC_CUDA(cudaMemsetAsync(partial_index, 0xff, count * sizeof(int64_t), stream()));
+        return VC_OK;
+    }
+    MaxOut o{partial_value, reinterpret_cast<long long*>(partial_index), 0, continuation ? 1 : 0,
+             static_cast<long long>(index_base)};
+    launch_max(in, outer, length, inner, o);
+    VC_API_END
+}
+
+vc_status vc_cuda_binary_backward_partial(int op, const float* a, const size_t* a_shape, int a_rank,
+                                          const float* b, const size_t* b_shape, int b_rank,
+                                          const float* g, const size_t* g_shape, int g_rank,
+                                          double* da_partial, double* db_partial) {
+    VC_API_BEGIN
+    ensure_init();
+    validate_rank(a_rank, "binary_backward_partial");
+    validate_rank(b_rank, "binary_backward_partial");
+    validate_rank(g_rank, "binary_backward_partial");
+    if (op < VC_ADD || op > VC_DIV) fail(VC_ERR_INVALID, "unknown binary operation");
+    const int rank = std::max(a_rank, b_rank);
+    size_t src[kMaxRank];
+    for (int i = 0; i < rank; ++i) {
+        const size_t ad = i < rank - a_rank ? 1 : a_shape[i - (rank - a_rank)];
+        const size_t bd = i < rank - b_rank ? 1 : b_shape[i - (rank - b_rank)];
+        if (ad != bd && ad != 1 && bd != 1) fail(VC_ERR_INVALID, "binary_backward_partial: shapes do not broadcast");
+        src[i] = std::max(ad, bd);
+    }
+    if (!g) fail(VC_ERR_INVALID, "binary_backward_partial: null gradient");
+    if (checked_numel(src, rank) == 0) {
+        if (da_partial) VC_CUDA(cudaMemsetAsync(da_partial, 0, checked_numel(a_shape, a_rank) * sizeof(double), stream()));
+        if (db_partial) VC_CUDA(cudaMemsetAsync(db_partial, 0, checked_numel(b_shape, b_rank) * sizeof(double), stream()));
+        return VC_OK;
+    }
+    const Src sg = align(g, g_shape, g_rank, src, rank, "binary_backward_partial");
+    const Src sa = align(a, a_shape, a_rank, src, rank, "binary_backward_partial");
+    const Src sb = align(b, b_shape, b_rank, src, rank, "binary_backward_partial");
+    if (da_partial) {
+        Src ops[3] = {sg, sb, sb};
+        const int f = (op == VC_ADD || op == VC_SUB) ? V_G : (op == VC_MUL ? V_MUL : V_DIV_A);
+        vjp_reduce(f, ops, src, rank, a_shape, a_rank, nullptr, 0.0f, da_partial);
+    }
+    if (db_partial) {
+        Src ops[3] = {sg, sa, sb};
+        const int f = op == VC_ADD ? V_G : (op == VC_SUB ? V_NEG : (op == VC_MUL ? V_MUL : V_DIV_B));
+        vjp_reduce(f, ops, src, rank, b_shape, b_rank, nullptr, 0.0f, db_partial);
+    }
+    VC_API_END
+}
+
+vc_status vc_cuda_combine_partials(int op, const double* partial_sum, const float* partial_value,
+                                   const int64_t* partial_index, int nranks, size_t count, float divisor,
+                                   int negate, float* out_value, int64_t* out_index) {
+    VC_API_BEGIN
+    ensure_init();
+    if (nranks <= 0) fail(VC_ERR_INVALID, "combine_partials: nranks must be positive");
+    if (!count) return VC_OK;
+    const unsigned grid = grid_for(count, kThreads);
+    if (op == VC_REDUCE_SUM || op == VC_REDUCE_MEAN) {
+        if (!partial_sum || !out_value) fail(VC_ERR_INVALID, "combine_partials: null pointer");
+        combine_sum_kernel<<<grid, kThreads, 0, stream()>>>(partial_sum, nranks, count, divisor, negate, out_value);
+    } else if (op == VC_REDUCE_MAX || op == VC_REDUCE_ARGMAX) {
+        if (!partial_value || !partial_index) fail(VC_ERR_INVALID, "combine_partials: null pointer");
+        combine_max_kernel<<<grid, kThreads, 0, stream()>>>(partial_value, reinterpret_cast<const long long*>(partial_index),
+                                                           nranks, count, op == VC_REDUCE_ARGMAX, out_value,
+                                                           reinterpret_cast<long long*>(out_index));
+    } else {
+        fail(VC_ERR_INVALID, "unknown reduction");
+    }
+    check_launch("combine_partials");
     VC_API_END
 }
 

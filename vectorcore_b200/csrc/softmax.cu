@@ -10,8 +10,8 @@
 // row, C in {1, 2, 4, 8} chosen so a CTA's slice of the row is at most 8K
 // floats (32 KB) -- small enough for several CTAs per SM so one CTA's loads
 // overlap another's arithmetic. Each CTA stages its slice in shared memory
-// with one TMA bulk copy (cp.async.bulk, completion on an mbarrier; no
-// multicast), reduces it, and the C partials are exchanged through
+// with one TMA bulk copy of its own slice (cp.async.bulk into its own shared
+// memory, completion on an mbarrier), reduces it, and the C partials are exchanged through
 // distributed shared memory and combined in rank order, so every CTA of the
 // cluster derives the same row statistics. Other axes (and rows too long for
 // a cluster) take a column kernel that walks the axis in global memory.
@@ -101,40 +101,75 @@ struct RowArgs {
     unsigned* err;
 };
 
-__device__ __forceinline__ MaxCand cluster_max(cg::cluster_group& cluster, MaxCand mine, float* s_v, long long* s_i,
-                                               unsigned C) {
-    if (threadIdx.x == 0) { *s_v = mine.v; *s_i = mine.i; }
-    cluster.sync();
-    MaxCand c{0.0f, -1};
-    for (unsigned r = 0; r < C; ++r) {
-        const float v = *cluster.map_shared_rank(s_v, r);
-        const long long i = *cluster.map_shared_rank(s_i, r);
-        c = max_combine(c, MaxCand{v, i});
-    }
-    return c;
-}
-
-__device__ __forceinline__ double cluster_sum(cg::cluster_group& cluster, double mine, double* s_d, unsigned C) {
-    if (threadIdx.x == 0) *s_d = mine;
-    cluster.sync();
-    double t = 0.0;
-    for (unsigned r = 0; r < C; ++r) t += *cluster.map_shared_rank(s_d, r);
+// ---- block / cluster combines (fixed order: the same result in every CTA) ----
+__device__ __forceinline__ float block_fmax(float v, float* scratch) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, m));
+    __syncthreads();
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    float t = lane < nw ? scratch[lane] : -INFINITY;
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) t = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, m));
     return t;
 }
 
+__device__ __forceinline__ unsigned long long block_umin(unsigned long long v, unsigned long long* scratch) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, m));
+    __syncthreads();
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    unsigned long long t = lane < nw ? scratch[lane] : ~0ull;
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) t = min(t, __shfl_xor_sync(0xffffffffu, t, m));
+    return t;
+}
+
+__device__ __forceinline__ float cluster_fmax(cg::cluster_group& cluster, float mine, float* slot, unsigned C) {
+    if (threadIdx.x == 0) *slot = mine;
+    cluster.sync();
+    float m = -INFINITY;
+    for (unsigned r = 0; r < C; ++r) m = fmaxf(m, *cluster.map_shared_rank(slot, r));
+    return m;
+}
+
+__device__ __forceinline__ unsigned long long cluster_umin(cg::cluster_group& cluster, unsigned long long mine,
+                                                           unsigned long long* slot, unsigned C) {
+    if (threadIdx.x == 0) *slot = mine;
+    cluster.sync();
+    unsigned long long m = ~0ull;
+    for (unsigned r = 0; r < C; ++r) m = min(m, *cluster.map_shared_rank(slot, r));
+    return m;
+}
+
+__device__ __forceinline__ double cluster_sum(cg::cluster_group& cluster, double mine, double* slot, unsigned C) {
+    if (threadIdx.x == 0) *slot = mine;
+    cluster.sync();
+    double t = 0.0;
+    for (unsigned r = 0; r < C; ++r) t += *cluster.map_shared_rank(slot, r);
+    return t;
+}
+
+__device__ __forceinline__ float4 ld_smem4(const float* s, unsigned j) { return reinterpret_cast<const float4*>(s)[j]; }
+
 // One cluster per row. Dynamic shared memory: [slice of x][slice of g].
+// BULK: the slice was staged with a TMA bulk copy, and the row length, the
+// slice start and the slice length are multiples of 4, so every pass is
+// float4-wide (shared and global).
 template <int MODE, bool BULK>
 __global__ void __launch_bounds__(kThreads)
 row_kernel(const RowArgs a, unsigned long long row0) {
     extern __shared__ __align__(128) float smem[];
     __shared__ unsigned long long bar;
     __shared__ double s_red[32];
-    __shared__ float s_mv[32];
-    __shared__ long long s_mi[32];
-    __shared__ float x_mv;          // cluster exchange slots (one per phase)
-    __shared__ long long x_mi;
+    __shared__ float s_f[32];
+    __shared__ unsigned long long s_u[32];
+    __shared__ float x_max;               // cluster exchange slots, one per phase
+    __shared__ unsigned long long x_idx;
     __shared__ double x_sum;
-    __shared__ double x_sum2;
 
     cg::cluster_group cluster = cg::this_cluster();
     const unsigned C = cluster.num_blocks();
@@ -142,17 +177,19 @@ row_kernel(const RowArgs a, unsigned long long row0) {
     const unsigned long long row = row0 + blockIdx.x / C;
     if (row >= a.rows) return;  // whole cluster exits together (same row)
 
-    constexpr bool STAGE_X = MODE == LSM_FWD || MODE == SM_FWD || MODE == CE_FWD || MODE == SM_BWD;
+    constexpr bool FWD = MODE == LSM_FWD || MODE == SM_FWD || MODE == CE_FWD;
+    constexpr bool STAGE_X = FWD || MODE == SM_BWD;
     constexpr bool STAGE_G = MODE == LSM_BWD || MODE == SM_BWD;
     const unsigned long long c0 = static_cast<unsigned long long>(rank) * a.seg;
     const unsigned n = c0 < a.L ? static_cast<unsigned>(min(static_cast<unsigned long long>(a.seg), a.L - c0)) : 0u;
+    const unsigned n4 = n / 4;
     float* sx = smem;
     float* sg = smem + (STAGE_X ? a.seg : 0);
     const float* xrow = a.x + row * a.L + c0;
-    const float* grow = STAGE_G || MODE == LSM_BWD ? a.g + row * a.L + c0 : nullptr;
+    const float* grow = STAGE_G ? a.g + row * a.L + c0 : nullptr;
+    float* yrow = a.y ? a.y + row * a.L + c0 : nullptr;
 
-    // ---- stage the slice(s) ------------------------------------------------
-    bool staged = true;
+    // ---- stage the slice(s) -----------------------------------------------------
     if constexpr (BULK) {
         const unsigned bytes = n * 4u * ((STAGE_X ? 1u : 0u) + (STAGE_G ? 1u : 0u));
         if (threadIdx.x == 0) {
@@ -165,7 +202,7 @@ row_kernel(const RowArgs a, unsigned long long row0) {
             if (STAGE_X) bulk_load(sx, xrow, n * 4u, &bar);
             if (STAGE_G) bulk_load(sg, grow, n * 4u, &bar);
         }
-        if (bytes) staged = mbar_wait_bounded(&bar, 0, a.err);
+        if (bytes) mbar_wait_bounded(&bar, 0, a.err);
     } else {
         for (unsigned k = threadIdx.x; k < n; k += kThreads) {
             if (STAGE_X) sx[k] = __ldg(xrow + k);
@@ -174,20 +211,42 @@ row_kernel(const RowArgs a, unsigned long long row0) {
         __syncthreads();
     }
 
-    float m, s;
-    if constexpr (MODE == LSM_FWD || MODE == SM_FWD || MODE == CE_FWD) {
-        // ---- row max (scan semantics) ----
-        MaxCand c{0.0f, -1};
-        for (unsigned k = threadIdx.x; k < n; k += kThreads) c = max_take(c, sx[k], static_cast<long long>(c0 + k));
-        c = block_max(c, s_mv, s_mi);
-        c = cluster_max(cluster, c, &x_mv, &x_mi, C);
+    if constexpr (FWD) {
+        // ---- row max m: fmaxf skips NaN; then the scan's exact rules ------------
+        float mloc = -INFINITY;
+        if constexpr (BULK) {
+            for (unsigned j = threadIdx.x; j < n4; j += kThreads) {
+                const float4 v = ld_smem4(sx, j);
+                mloc = fmaxf(mloc, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
+            }
+        } else {
+            for (unsigned k = threadIdx.x; k < n; k += kThreads) mloc = fmaxf(mloc, sx[k]);
+        }
+        float m = cluster_fmax(cluster, block_fmax(mloc, s_f), &x_max, C);
         const float first = __ldg(a.x + row * a.L);
-        m = first != first ? first : c.v;
-        // ---- row sum of expf(x - m), double ----
-        double acc = 0.0;
-        for (unsigned k = threadIdx.x; k < n; k += kThreads) acc += static_cast<double>(expf(sx[k] - m));
-        acc = block_sum(acc, s_red);
-        s = static_cast<float>(cluster_sum(cluster, acc, &x_sum, C));
+        if (first != first) {
+            m = first;  // the scan never leaves a NaN at index 0
+        } else if (m == 0.0f) {
+            // a zero maximum is the FIRST zero of the row (its sign matters);
+            // the condition is the same in every CTA of the cluster
+            unsigned long long idx = ~0ull;
+            for (unsigned k = threadIdx.x; k < n; k += kThreads)
+                if (sx[k] == 0.0f) { idx = c0 + k; break; }
+            idx = cluster_umin(cluster, block_umin(idx, s_u), &x_idx, C);
+            m = __ldg(a.x + row * a.L + idx);
+        }
+        // ---- s = float(double sum of expf(x - m)) ----
+        double acc0 = 0.0, acc1 = 0.0;
+        if constexpr (BULK) {
+            for (unsigned j = threadIdx.x; j < n4; j += kThreads) {
+                const float4 v = ld_smem4(sx, j);
+                acc0 += static_cast<double>(expf(v.x - m)) + static_cast<double>(expf(v.y - m));
+                acc1 += static_cast<double>(expf(v.z - m)) + static_cast<double>(expf(v.w - m));
+            }
+        } else {
+            for (unsigned k = threadIdx.x; k < n; k += kThreads) acc0 += static_cast<double>(expf(sx[k] - m));
+        }
+        const float s = static_cast<float>(cluster_sum(cluster, block_sum(acc0 + acc1, s_red), &x_sum, C));
         const float l = logf(s);
         if (rank == 0 && threadIdx.x == 0) {
             if (a.row_max) a.row_max[row] = m;
@@ -202,43 +261,78 @@ row_kernel(const RowArgs a, unsigned long long row0) {
                 a.row_term[row] = (sx[t - c0] - m) - l;
             }
         } else {
-            float* yrow = a.y + row * a.L + c0;
-            for (unsigned k = threadIdx.x; k < n; k += kThreads) {
-                const float ls = (sx[k] - m) - l;
-                yrow[k] = MODE == SM_FWD ? expf(ls) : ls;
+            auto f = [&](float v) {
+                const float ls = (v - m) - l;
+                return MODE == SM_FWD ? expf(ls) : ls;
+            };
+            if constexpr (BULK) {
+                for (unsigned j = threadIdx.x; j < n4; j += kThreads) {
+                    const float4 v = ld_smem4(sx, j);
+                    st4_stream(yrow + 4 * j, make_float4(f(v.x), f(v.y), f(v.z), f(v.w)));
+                }
+            } else {
+                for (unsigned k = threadIdx.x; k < n; k += kThreads) yrow[k] = f(sx[k]);
             }
         }
     } else {
-        m = __ldg(a.row_max + row);
-        s = __ldg(a.row_sum + row);
+        const float m = __ldg(a.row_max + row);
+        const float s = __ldg(a.row_sum + row);
         if constexpr (MODE == LSM_BWD) {
-            double acc = 0.0;
-            for (unsigned k = threadIdx.x; k < n; k += kThreads) acc += static_cast<double>(-sg[k]);
-            acc = block_sum(acc, s_red);
-            const float dl = static_cast<float>(cluster_sum(cluster, acc, &x_sum, C));
-            const float ds = dl / s;
-            const float de = ds + 0.0f;
-            float* dxrow = a.y + row * a.L + c0;
-            for (unsigned k = threadIdx.x; k < n; k += kThreads)
-                dxrow[k] = sg[k] + de * expf(__ldg(xrow + k) - m);
-        } else {  // SM_BWD
-            const float l = logf(s);
-            double acc = 0.0;
-            for (unsigned k = threadIdx.x; k < n; k += kThreads) {
-                const float y = expf((sx[k] - m) - l);
-                const float gy = sg[k] * y;
-                sg[k] = gy;
-                acc += static_cast<double>(-gy);
+            // dx = g + ((float(sum(-g)) / s) + 0) * expf(x - m)
+            double acc0 = 0.0, acc1 = 0.0;
+            if constexpr (BULK) {
+                for (unsigned j = threadIdx.x; j < n4; j += kThreads) {
+                    const float4 g = ld_smem4(sg, j);
+                    acc0 += static_cast<double>(-g.x) + static_cast<double>(-g.y);
+                    acc1 += static_cast<double>(-g.z) + static_cast<double>(-g.w);
+                }
+            } else {
+                for (unsigned k = threadIdx.x; k < n; k += kThreads) acc0 += static_cast<double>(-sg[k]);
             }
-            acc = block_sum(acc, s_red);
-            const float dl = static_cast<float>(cluster_sum(cluster, acc, &x_sum2, C));
-            const float ds = dl / s;
-            const float de = ds + 0.0f;
-            float* dxrow = a.y + row * a.L + c0;
-            for (unsigned k = threadIdx.x; k < n; k += kThreads) dxrow[k] = sg[k] + de * expf(sx[k] - m);
+            const float dl = static_cast<float>(cluster_sum(cluster, block_sum(acc0 + acc1, s_red), &x_sum, C));
+            const float de = (dl / s) + 0.0f;
+            if constexpr (BULK) {
+                for (unsigned j = threadIdx.x; j < n4; j += kThreads) {
+                    const float4 g = ld_smem4(sg, j);
+                    const float4 x = ld4_stream(xrow + 4 * j);
+                    st4_stream(yrow + 4 * j, make_float4(g.x + de * expf(x.x - m), g.y + de * expf(x.y - m),
+                                                         g.z + de * expf(x.z - m), g.w + de * expf(x.w - m)));
+                }
+            } else {
+                for (unsigned k = threadIdx.x; k < n; k += kThreads) yrow[k] = sg[k] + de * expf(__ldg(xrow + k) - m);
+            }
+        } else {  // SM_BWD: gy = g * y; dx = gy + ((float(sum(-gy)) / s) + 0) * expf(x - m)
+            const float l = logf(s);
+            double acc0 = 0.0, acc1 = 0.0;
+            auto gy_of = [&](float x, float g) { return g * expf((x - m) - l); };
+            if constexpr (BULK) {
+                for (unsigned j = threadIdx.x; j < n4; j += kThreads) {
+                    const float4 x = ld_smem4(sx, j), g = ld_smem4(sg, j);
+                    const float4 gy = make_float4(gy_of(x.x, g.x), gy_of(x.y, g.y), gy_of(x.z, g.z), gy_of(x.w, g.w));
+                    reinterpret_cast<float4*>(sg)[j] = gy;
+                    acc0 += static_cast<double>(-gy.x) + static_cast<double>(-gy.y);
+                    acc1 += static_cast<double>(-gy.z) + static_cast<double>(-gy.w);
+                }
+            } else {
+                for (unsigned k = threadIdx.x; k < n; k += kThreads) {
+                    const float gy = gy_of(sx[k], sg[k]);
+                    sg[k] = gy;
+                    acc0 += static_cast<double>(-gy);
+                }
+            }
+            const float dl = static_cast<float>(cluster_sum(cluster, block_sum(acc0 + acc1, s_red), &x_sum, C));
+            const float de = (dl / s) + 0.0f;
+            if constexpr (BULK) {
+                for (unsigned j = threadIdx.x; j < n4; j += kThreads) {
+                    const float4 x = ld_smem4(sx, j), gy = ld_smem4(sg, j);
+                    st4_stream(yrow + 4 * j, make_float4(gy.x + de * expf(x.x - m), gy.y + de * expf(x.y - m),
+                                                         gy.z + de * expf(x.z - m), gy.w + de * expf(x.w - m)));
+                }
+            } else {
+                for (unsigned k = threadIdx.x; k < n; k += kThreads) yrow[k] = sg[k] + de * expf(sx[k] - m);
+            }
         }
     }
-    (void)staged;
     // Keep this CTA's shared memory alive until every rank has read it.
     cluster.sync();
 }
