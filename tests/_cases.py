@@ -82,6 +82,11 @@ BROADCAST_CASES = [
     ((40, 1, 300), (1, 50, 300)),
     ((40, 50, 1), (50, 7)),
     ((3,), (2, 1)),
+    # long rows (the warp-per-row path): two leading dims, a row-constant
+    # operand, and rows long enough for its four-deep unrolled loop
+    ((16, 1, 1000), (1, 9, 1000)),
+    ((5, 7, 1, 2052), (7, 3, 2052)),
+    ((60, 1), (1, 1028)),
 ]
 
 # sum_to_shape layouts (tests/python/test_performance_paths.py:162-176) plus

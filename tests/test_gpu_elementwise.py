@@ -139,6 +139,61 @@ def test_binary_backward(backend, port, a_shape, b_shape):
                 assert_sum_close(got, ref, n, 1.0, what=f"{name} grad {shape} of {out_shape}")
 
 
+# Two-sided broadcasts: both gradients reduce, from one pass over g. Cases
+# cover V (the dims only b spans) = 128, a non-power-of-two V, a partial
+# 32-float chunk of the inner run, two a-only and two b-only dims
+# interleaved, an outer dim both operands span, and enough a-only positions
+# for many U segments.
+FUSED_CASES = [((8, 1, 64, 256), (1, 128, 1, 256)), ((16, 1, 40, 64), (1, 3, 1, 64)),
+               ((4, 1, 50, 96), (1, 100, 1, 96)), ((7, 1, 33, 36), (1, 9, 1, 36)),
+               ((1, 6, 1, 10, 16), (4, 1, 5, 1, 16)), ((5, 3, 1, 128), (5, 1, 2, 128)),
+               ((64, 1, 512, 64), (1, 16, 1, 64))]
+
+
+@pytest.mark.parametrize("a_shape,b_shape", FUSED_CASES)
+def test_binary_backward_two_sided_broadcast(backend, port, a_shape, b_shape):
+    rng = np.random.default_rng(int(np.prod(a_shape)) % 997)
+    a = rng.uniform(0.5, 2, size=a_shape).astype(np.float32)
+    b = rng.uniform(0.5, 2, size=b_shape).astype(np.float32)
+    out_shape = np.broadcast_shapes(a_shape, b_shape)
+    g = rng.uniform(-1, 1, size=out_shape).astype(np.float32)
+    da_, db_, dg = dev(backend, a), dev(backend, b), dev(backend, g)
+    for name, op in OPS.items():
+        ga, gb = backend.binary_backward(op, da_, a_shape, db_, b_shape, dg, out_shape)
+        ra, rb = port.binary_backward(op, a, b, g)
+        for got_s, ref, shape in ((ga, ra, a_shape), (gb, rb, b_shape)):
+            n = int(np.prod(out_shape)) // int(np.prod(shape))
+            assert_sum_close(host(backend, got_s, shape), ref, n, 1.0, what=f"{name} grad {shape} of {out_shape}")
+    backend.synchronize()  # no bounded wait gave up
+
+
+def test_binary_backward_partial_two_sided(backend, port):
+    """The shard-partial entry point returns the unrounded double sums of the
+    same fused pass."""
+    import ctypes
+
+    from vectorcore_b200 import _abi
+
+    a_shape, b_shape = (16, 1, 40, 64), (1, 24, 1, 64)
+    rng = np.random.default_rng(3)
+    a = rng.uniform(0.5, 2, size=a_shape).astype(np.float32)
+    b = rng.uniform(0.5, 2, size=b_shape).astype(np.float32)
+    out_shape = np.broadcast_shapes(a_shape, b_shape)
+    g = rng.uniform(-1, 1, size=out_shape).astype(np.float32)
+    da_, db_, dg = dev(backend, a), dev(backend, b), dev(backend, g)
+    pa = backend.allocate(2 * a.size)  # room for a.size doubles
+    pb = backend.allocate(2 * b.size)
+    shp = lambda s: (ctypes.c_size_t * len(s))(*s)
+    _abi.call("vc_cuda_binary_backward_partial", B.MUL, ctypes.c_void_p(da_.ptr), shp(a_shape), len(a_shape),
+              ctypes.c_void_p(db_.ptr), shp(b_shape), len(b_shape), ctypes.c_void_p(dg.ptr), shp(out_shape),
+              len(out_shape), ctypes.c_void_p(pa.ptr), ctypes.c_void_p(pb.ptr))
+    got_a = backend.download(pa).view(np.float64).reshape(a_shape)
+    got_b = backend.download(pb).view(np.float64).reshape(b_shape)
+    ra, rb = port.binary_backward(B.MUL, a, b, g)
+    assert_sum_close(got_a.astype(np.float32), ra, 24, 1.0, what="da partial")
+    assert_sum_close(got_b.astype(np.float32), rb, 640, 1.0, what="db partial")
+
+
 def test_binary_backward_scalar_upstream(backend, port):
     # sum() backward hands a 0-d gradient; the kernel reads it broadcast.
     a, b = C.cfg5(C.SMALL["cfg5"]["a"], C.SMALL["cfg5"]["b"])

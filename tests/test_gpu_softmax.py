@@ -32,7 +32,9 @@ def split(shape, axis):
 
 CASES = [((6, 5), -1), ((6, 5), 0), ((3, 7, 9), 1), ((37, 45), 0), ((64, 1000), -1), ((16, 8191), -1),
          ((8, 9000), -1), ((4, 20000), -1), ((4, 32000), -1), ((2, 70000), -1), ((2, 196608), -1),
-         ((2, 200003), -1), ((3, 33), -1), ((1, 1), -1)]
+         ((2, 200003), -1), ((3, 33), -1), ((1, 1), -1),
+         # thousands of rows: many clusters per SM, every cluster size
+         ((3000, 1000), -1), ((700, 9000), -1), ((1200, 32000), -1), ((300, 70000), -1), ((2500, 33), -1)]
 
 
 @pytest.mark.parametrize("shape,axis", CASES)
@@ -51,6 +53,45 @@ def test_softmax_family(backend, port, shape, axis):
         assert_rel(backend.download(gx).reshape(shape), refb, RTOL, f"backward {shape}", scale=np.abs(g).max())
     _, pm, ps = port.log_softmax(x, axis, stats=True)
     assert np.array_equal(backend.download(m), pm)  # the row max is exact
+    # the row sums' exp terms come from an ex2-based exp (a few float ulps a
+    # term): the sum stays within 2e-6 of the reference's double sum of expf
+    np.testing.assert_allclose(backend.download(s), ps, rtol=2e-6, atol=0)
+
+
+@pytest.mark.parametrize("length", [1024, 32000])
+def test_softmax_edge_rows_among_many(backend, port, length):
+    """Rows with the scan's special cases (a zero maximum whose first zero is
+    -0.0, NaN at index 0, NaN elsewhere, -inf, +-1000) scattered among
+    thousands of ordinary rows, in CTAs other than the first of a cluster."""
+    rows = 3000 if length == 1024 else 400
+    rng = np.random.default_rng(length)
+    x = rng.normal(0, 2, size=(rows, length)).astype(np.float32)
+    x[5] = 0.0
+    x[5, : length // 3] = -5.0
+    x[5, length // 3] = -0.0            # the first zero is negative
+    x[6] = -0.0
+    x[6, length - 1] = 0.0
+    x[7, 0] = np.nan                    # NaN at index 0 wins the max
+    x[rows // 2, length - 3] = np.nan   # NaN elsewhere: skipped by the max, poisons the sum
+    x[rows - 1, ::7] = -np.inf
+    x[rows - 2, 1] = 1000.0
+    x[rows - 2, length - 2] = -1000.0
+    x[rows - 3] = 0.0                   # all +0.0
+    g = rng.uniform(-1, 1, size=x.shape).astype(np.float32)
+    dx, dg = dev(backend, x), dev(backend, g)
+    with np.errstate(invalid="ignore"):
+        for log in (True, False):
+            y, m, s = backend.softmax(dx, rows, length, 1, log=log)
+            ref = port.log_softmax(x, -1) if log else port.softmax(x, -1)
+            assert_rel(backend.download(y).reshape(x.shape), ref, RTOL, f"{'log_' if log else ''}softmax edges")
+            gx = backend.softmax_backward(dx, m, s, dg, rows, length, 1, log=log)
+            refb = port.log_softmax_backward(x, g, -1) if log else port.softmax_backward(x, g, -1)
+            assert_rel(backend.download(gx).reshape(x.shape), refb, RTOL, "backward edges", scale=1.0)
+    _, pm, _ = port.log_softmax(x, -1, stats=True)
+    got_m = backend.download(m)
+    same = (got_m.view(np.uint32) == pm.view(np.uint32)) | (np.isnan(got_m) & np.isnan(pm))
+    assert same.all(), np.flatnonzero(~same)[:10]
+    assert got_m.view(np.uint32)[5] == np.float32(-0.0).view(np.uint32)
 
 
 def test_softmax_rows_sum_to_one_and_huge_logits(backend, golden):

@@ -6,11 +6,12 @@
 //  * flat paths (same shape, scalar operand): 128-bit loads/stores, four
 //    independent float4 per thread per iteration, grid = a multiple of the SM
 //    count with a grid-stride loop;
-//  * every other broadcast layout: dimensions are collapsed on the host, the
-//    innermost run of L elements is a "row", and each CTA resolves the operand
-//    offsets of a tile of rows ONCE into shared memory (what the reference's
-//    CPU kernel does per row, src/cpu/cpu_backend.cpp:59-105) and then streams
-//    the tile, 128-bit wide when the row layout allows. Offsets are 64-bit:
+//  * every other broadcast layout: dimensions are collapsed on the host and
+//    the innermost run of L elements is a "row" (what the reference's CPU
+//    kernel resolves per row, src/cpu/cpu_backend.cpp:59-105). Long float4
+//    rows (L >= 128) take one warp per row, offsets decoded with FastDiv in
+//    registers; other layouts resolve the operand offsets of a tile of rows
+//    once into shared memory and then stream the tile. Offsets are 64-bit:
 //    config 5 has 2^32 outputs.
 // Arithmetic is the reference's (src/cpu/cpu_backend.cpp:24-27, 291-316),
 // compiled with -fmad=false and IEEE division so add/sub/mul/div/neg/relu
@@ -195,6 +196,66 @@ binary_tiled_kernel(const float* __restrict__ a, const float* __restrict__ b, fl
             }
         }
         __syncthreads();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Row-broadcast path for long rows (L >= 128, float4-aligned): one warp per
+// output row, no shared memory and no block barrier. Each lane decodes the
+// row's operand offsets with FastDiv (the same value in every lane, so no
+// shuffle is needed) and streams float4 groups with four loads in flight; an
+// operand constant along the row (inner stride 0) is read once per row.
+// ---------------------------------------------------------------------------
+struct RowsDesc {
+    int lead_rank;
+    FastDiv lead[kMaxRank];             // leading (row) dims, outer first
+    long long a_lead[kMaxRank], b_lead[kMaxRank];
+    long long a_inner, b_inner;         // 0 or 1
+    unsigned rows;                      // < 2^31
+    unsigned L4;                        // row length / 4
+};
+
+__device__ __forceinline__ float4 rows_fetch(const float* p, float v, long long inner, float per_row, unsigned j) {
+    if (!p) return make_float4(v, v, v, v);
+    if (inner == 0) return make_float4(per_row, per_row, per_row, per_row);
+    return ldg4(p + 4ull * j);
+}
+
+template <int OP>
+__global__ void __launch_bounds__(kThreads)
+binary_rows_kernel(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ out,
+                   const RowsDesc d, float av, float bv) {
+    const unsigned lane = threadIdx.x & 31;
+    const unsigned warps = (gridDim.x * blockDim.x) >> 5;
+    for (unsigned row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < d.rows; row += warps) {
+        unsigned r = row;
+        long long ao = 0, bo = 0;
+        for (int k = d.lead_rank - 1; k >= 0; --k) {
+            unsigned q, c;
+            d.lead[k].divmod(r, q, c);
+            r = q;
+            ao += static_cast<long long>(c) * d.a_lead[k];
+            bo += static_cast<long long>(c) * d.b_lead[k];
+        }
+        const float* ar = a ? a + ao : nullptr;
+        const float* br = b ? b + bo : nullptr;
+        const float ar0 = ar && d.a_inner == 0 ? __ldg(ar) : 0.0f;
+        const float br0 = br && d.b_inner == 0 ? __ldg(br) : 0.0f;
+        float* orow = out + static_cast<std::size_t>(row) * d.L4 * 4;
+        unsigned j = lane;
+        for (; j + 96 < d.L4; j += 128) {
+            float4 x[4], y[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                x[u] = rows_fetch(ar, av, d.a_inner, ar0, j + 32 * u);
+                y[u] = rows_fetch(br, bv, d.b_inner, br0, j + 32 * u);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) st4_stream(orow + 4ull * (j + 32 * u), bop4<OP>(x[u], y[u]));
+        }
+        for (; j < d.L4; j += 32)
+            st4_stream(orow + 4ull * j, bop4<OP>(rows_fetch(ar, av, d.a_inner, ar0, j),
+                                                rows_fetch(br, bv, d.b_inner, br0, j)));
     }
 }
 
@@ -439,6 +500,28 @@ static void launch_binary_op(const Operand& a, const Operand& b, float* out, con
     };
     const bool vec = d.L % 4 == 0 && aligned16(out) && lead_ok(d.a_lead, d.a_inner, a.ptr) &&
                      lead_ok(d.b_lead, d.b_inner, b.ptr);
+    bool rows_ok = vec && d.L >= 128 && d.rows < (1ull << 31) && d.L / 4 < (1ull << 31) &&
+                   d.rows * (d.L / 4) < (1ull << 62);
+    for (int i = 0; i < d.lead_rank; ++i) rows_ok = rows_ok && d.lead_dims[i] < (1ull << 31);
+    if (rows_ok) {
+        RowsDesc rd{};
+        rd.lead_rank = d.lead_rank;
+        for (int i = 0; i < d.lead_rank; ++i) {
+            rd.lead[i] = FastDiv(static_cast<unsigned>(d.lead_dims[i]));
+            rd.a_lead[i] = d.a_lead[i];
+            rd.b_lead[i] = d.b_lead[i];
+        }
+        rd.a_inner = a.ptr ? d.a_inner : 0;
+        rd.b_inner = b.ptr ? d.b_inner : 0;
+        rd.rows = static_cast<unsigned>(d.rows);
+        rd.L4 = static_cast<unsigned>(d.L / 4);
+        const std::size_t warps_per_cta = kThreads / 32;
+        const std::size_t ctas = (d.rows + warps_per_cta - 1) / warps_per_cta;
+        const unsigned grid = static_cast<unsigned>(std::min<std::size_t>(ctas, static_cast<std::size_t>(sm_count()) * 16));
+        binary_rows_kernel<OP><<<grid, kThreads, 0, s>>>(a.ptr, b.ptr, out, rd, a.value, b.value);
+        check_launch("binary_rows");
+        return;
+    }
     const std::size_t tiles = (d.rows + d.tile_rows - 1) / d.tile_rows * d.col_chunks;
     const unsigned grid = static_cast<unsigned>(std::min<std::size_t>(tiles, static_cast<std::size_t>(sm_count()) * 8));
     if (vec) binary_tiled_kernel<OP, true><<<grid, kThreads, 0, s>>>(a.ptr, b.ptr, out, d, a.value, b.value);

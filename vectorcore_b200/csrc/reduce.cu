@@ -16,8 +16,12 @@
 // SM count), so results do not depend on the launch configuration.
 #include "vc_internal.cuh"
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <algorithm>
 #include <cstring>
+#include <mutex>
 
 namespace vc {
 
@@ -582,6 +586,499 @@ binary_backward_flat(const float* __restrict__ a, const float* __restrict__ b, c
 }
 
 // ---------------------------------------------------------------------------
+// Two-sided broadcast backward from ONE read of a dense upstream g.
+//
+// When a and b are both broadcast (out = a * b with a [P,1,R,L] and
+// b [1,Q,1,L], say), each needs its own reduction of g: da over the dims
+// where a has extent 1, db over the dims where b has. The reference runs one
+// full pass per reduced axis for each (src/autograd.cpp:50-72 after
+// src/ops.cpp:124-156). Canonical layout after dropping unit dims and merging
+// neighbours of one class:
+//   L -- the innermost run, kept by both gradients (float4 lanes);
+//   U -- the dims only a spans (da keeps them, db reduces them), at most two;
+//   V -- the dims only b spans (db keeps them, da reduces them), V <= 128;
+//   K -- outer dims both span (independent problems, grid.z), at most two.
+// A CTA owns 32 floats of L (one 128-byte line of every row), all V and a
+// segment of U. TMA streams, per u, the [V][32] tile of g and the [32] line
+// of a into a ring of kFStages shared-memory stages (tensor maps over g and
+// a; the copy engine keeps the next steps in flight while the CTA computes).
+// The 512 threads form 64 "slots" of 8 float4 lanes; slot s = (vs, us) takes
+// v = vs + VS*i (its b values live in registers) and the u of tile us of each
+// step. Per step every slot
+//   * folds the vjp_a terms of its v's (float, in i order: at most 2) into one
+//     value per lane; the VS slots of a u are then combined in a fixed tree
+//     (float within a thread's share, double across threads) and da is
+//     written, rounded once;
+//   * adds the vjp_b terms into a per-(v, lane) float block that is flushed
+//     every 8 steps into double accumulators in shared memory; at the end the
+//     US groups are combined in order into db (or into this U segment's
+//     partial, summed in segment order by reduce_col_finish).
+// Every combine order depends on the shape only. The float blocks (at most 8
+// terms) add a relative error of a few float ulps of the block; the
+// reference's sums round once per axis, so both sit well inside the sum
+// tolerance.
+// ---------------------------------------------------------------------------
+constexpr unsigned kFThreads = 512;
+constexpr unsigned kFLanes = 8;                 // float4 lanes per slot
+constexpr unsigned kFSlots = kFThreads / kFLanes;
+constexpr unsigned kFChunk = kFLanes * 4;       // floats of L per CTA
+constexpr unsigned kFMaxV = 128;
+constexpr unsigned kFMaxNV = kFMaxV / kFSlots;
+constexpr unsigned kFStages = 3;
+constexpr unsigned kFFlush = 8;                 // steps per float block of db
+// CTAs to aim for: 8 waves of 148 SMs x 2 resident CTAs (a constant: the
+// split, and so the result, depends on the shape alone).
+constexpr unsigned long long kFTargetCtas = 148ull * 2 * 8;
+constexpr unsigned long long kFMinUSeg = 128;
+constexpr std::size_t kFMaxSmem = 112 * 1024;
+
+struct FusedDesc {
+    int rank_g, rank_a;          // tensor-map ranks
+    int ucoord_g, ucoord_a;      // coordinate index of U1 in each map (then U0, then K)
+    int has_u0, nk;
+    unsigned U0, U1;
+    FastDiv u1fd;
+    long long ua0, ua1;          // da (= a layout) strides of the U dims
+    unsigned long long kdims[2]; // K dims, outer first
+    long long ka[2], kb[2];      // da / db strides of the K dims
+    int nv;
+    unsigned vdims[2];           // V dims, outer first
+    long long vb[2];             // db (= b layout) strides of the V dims
+    unsigned U, V;
+    unsigned long long L;        // innermost run, a multiple of 4
+    unsigned useg, S;            // u positions per segment, segments
+    unsigned VS, US, NV;         // slot split: v-slots, u-slots, v's per slot
+    unsigned vs_log2, tp_log2;   // log2 of VS and of the threads per da output
+    unsigned stage_bytes;        // one step: US tiles of g ([V][32]) and of a ([32])
+    unsigned long long db_count; // elements of db (the partial stride)
+    double* da_d;                // unrounded outputs (shard partials) when set
+    double* db_d;
+    unsigned* err;               // device error word (bounded waits)
+};
+
+// Tiled TMA load (no multicast) of one box into this CTA's shared memory.
+__device__ __forceinline__ void tma_load(void* dst, const CUtensorMap* map, int rank, const int* c,
+                                         unsigned long long* bar) {
+    const unsigned d = smem_addr(dst), b = smem_addr(bar);
+    const unsigned long long m = reinterpret_cast<unsigned long long>(map);
+    switch (rank) {
+        case 2:
+            asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                         " [%0], [%1, {%2, %3}], [%4];" ::"r"(d), "l"(m), "r"(c[0]), "r"(c[1]), "r"(b) : "memory");
+            break;
+        case 3:
+            asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                         " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(d), "l"(m), "r"(c[0]), "r"(c[1]), "r"(c[2]),
+                         "r"(b) : "memory");
+            break;
+        case 4:
+            asm volatile("cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                         " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(d), "l"(m), "r"(c[0]), "r"(c[1]), "r"(c[2]),
+                         "r"(c[3]), "r"(b) : "memory");
+            break;
+        default:
+            asm volatile("cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                         " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(d), "l"(m), "r"(c[0]), "r"(c[1]), "r"(c[2]),
+                         "r"(c[3]), "r"(c[4]), "r"(b) : "memory");
+            break;
+    }
+}
+
+__device__ __forceinline__ long long decode_vb(const FusedDesc& d, unsigned v) {
+    long long bo = 0;
+    for (int i = d.nv - 1; i >= 0; --i) {
+        const unsigned c = v % d.vdims[i];
+        v /= d.vdims[i];
+        bo += static_cast<long long>(c) * d.vb[i];
+    }
+    return bo;
+}
+
+__device__ __forceinline__ float4 add4(float4 x, float4 y) { return make_float4(x.x + y.x, x.y + y.y, x.z + y.z, x.w + y.w); }
+
+template <int OP>
+__global__ void __launch_bounds__(kFThreads, 2)
+bcast_backward_fused(const __grid_constant__ CUtensorMap gmap, const __grid_constant__ CUtensorMap amap,
+                     const float* __restrict__ b, const FusedDesc d, float* __restrict__ da,
+                     float* __restrict__ db, double* __restrict__ partial) {
+    constexpr bool NEED_A = OP == VC_MUL || OP == VC_DIV;
+    constexpr bool NEED_B = OP == VC_MUL || OP == VC_DIV;
+    // dynamic shared memory: [kFStages] steps of ([US][V][32] g, [US][32] a),
+    // [US][V][32] double db accumulators, [2][slots][32] float da partials
+    extern __shared__ __align__(1024) unsigned char fsm[];
+    const unsigned g_tile = d.V * kFChunk;  // floats of one g tile
+    double* dacc = reinterpret_cast<double*>(fsm + kFStages * d.stage_bytes);
+    const unsigned acc_count = d.US * d.V * kFChunk;
+    float* scratch = reinterpret_cast<float*>(dacc + acc_count);
+    __shared__ unsigned long long full[kFStages];
+    __shared__ long long s_uao[2][kFSlots];  // da offset of each u-slot's u, by step parity
+
+    const unsigned lane = threadIdx.x % kFLanes, slot = threadIdx.x / kFLanes;
+    const unsigned vs = slot & (d.VS - 1), us = slot >> d.vs_log2;
+    const unsigned long long l0 = static_cast<unsigned long long>(blockIdx.x) * kFChunk;
+    const bool lane_ok = l0 + lane * 4 < d.L;
+    const unsigned seg = blockIdx.y;
+    const unsigned u0 = seg * d.useg;
+    const unsigned u1 = min(d.U, u0 + d.useg);
+    const unsigned nsteps = (u1 - u0 + d.US - 1) / d.US;
+
+    // K position of this CTA: coordinates (outer first) and da / db offsets
+    int kc[2] = {0, 0};
+    long long ka = 0, kb = 0;
+    {
+        unsigned long long r = blockIdx.z;
+        for (int i = d.nk - 1; i >= 0; --i) {
+            const unsigned long long c = r % d.kdims[i];
+            r /= d.kdims[i];
+            kc[i] = static_cast<int>(c);
+            ka += static_cast<long long>(c) * d.ka[i];
+            kb += static_cast<long long>(c) * d.kb[i];
+        }
+    }
+    float4 breg[kFMaxNV];
+    bool vok[kFMaxNV];
+#pragma unroll
+    for (unsigned i = 0; i < kFMaxNV; ++i) {
+        const unsigned v = vs + d.VS * i;
+        vok[i] = i < d.NV && v < d.V;
+        breg[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (NEED_B && vok[i] && lane_ok)
+            breg[i] = ldg4(b + kb + decode_vb(d, v) + static_cast<long long>(l0 + lane * 4));
+    }
+    for (unsigned i = threadIdx.x; i < acc_count; i += kFThreads) dacc[i] = 0.0;
+    if (threadIdx.x == 0) {
+        for (unsigned s = 0; s < kFStages; ++s) mbar_init(&full[s], 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+
+    // producer (thread 0): step t -> stage t % kFStages, u = u0 + t*US + j
+    unsigned p_c1 = 0, p_c0 = 0;  // U coordinates of the next u to issue
+    unsigned issued = 0;          // steps issued
+    if (threadIdx.x == 0) d.u1fd.divmod(u0, p_c0, p_c1);
+    auto issue = [&](unsigned t) {
+        unsigned char* st = fsm + (t % kFStages) * d.stage_bytes;
+        const unsigned first = u0 + t * d.US;
+        const unsigned n = min(d.US, u1 - first);
+        mbar_expect_tx(&full[t % kFStages],
+                       n * (g_tile + (NEED_A ? kFChunk : 0u)) * static_cast<unsigned>(sizeof(float)));
+        for (unsigned j = 0; j < n; ++j) {
+            int cg_[5] = {static_cast<int>(l0), 0, 0, 0, 0};
+            int ca_[5] = {static_cast<int>(l0), 0, 0, 0, 0};
+            cg_[d.ucoord_g] = static_cast<int>(p_c1);
+            ca_[d.ucoord_a] = static_cast<int>(p_c1);
+            int ng = d.ucoord_g + 1, na = d.ucoord_a + 1;
+            if (d.has_u0) { cg_[ng++] = static_cast<int>(p_c0); ca_[na++] = static_cast<int>(p_c0); }
+            for (int i = d.nk - 1; i >= 0; --i) { cg_[ng++] = kc[i]; ca_[na++] = kc[i]; }  // innermost first
+            tma_load(reinterpret_cast<float*>(st) + j * g_tile, &gmap, d.rank_g, cg_, &full[t % kFStages]);
+            if (NEED_A)
+                tma_load(reinterpret_cast<float*>(st) + d.US * g_tile + j * kFChunk, &amap, d.rank_a, ca_,
+                         &full[t % kFStages]);
+            if (++p_c1 == d.U1) { p_c1 = 0; ++p_c0; }
+        }
+        ++issued;
+    };
+    if (threadIdx.x == 0)
+        for (unsigned t = 0; t < kFStages && t < nsteps; ++t) issue(t);
+
+    // da offset of this slot's u (slots with vs == 0 publish it per step)
+    unsigned c_c0, c_c1;
+    d.u1fd.divmod(u0 + us, c_c0, c_c1);
+    long long uao = static_cast<long long>(c_c0) * d.ua0 + static_cast<long long>(c_c1) * d.ua1;
+
+    float4 facc[kFMaxNV];
+#pragma unroll
+    for (unsigned i = 0; i < kFMaxNV; ++i) facc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    const unsigned tp = 1u << d.tp_log2, per = d.VS >> d.tp_log2;
+    // Only thread 0 polls a stage's mbarrier (512 threads polling one word
+    // would crowd the shared-memory pipe); the CTA barrier that follows
+    // publishes the stage, and the success flag, to every thread.
+    unsigned waited = 0;  // steps thread 0 has seen complete
+    bool ok = true;
+    if (threadIdx.x == 0 && nsteps > 0) {
+        ok = mbar_wait_bounded(&full[0], 0u, d.err);
+        waited = ok ? 1u : 0u;
+    }
+    ok = __syncthreads_and(ok) != 0;
+    unsigned u = u0 + us;
+    for (unsigned t = 0; t < nsteps; ++t, u += d.US) {
+        const unsigned stg = t % kFStages;
+        const float* sg = reinterpret_cast<const float*>(fsm + stg * d.stage_bytes);
+        float4 dap = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (u < u1 && lane_ok) {
+            const float4 av = NEED_A ? reinterpret_cast<const float4*>(sg + d.US * g_tile + us * kFChunk)[lane]
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (unsigned i = 0; i < kFMaxNV; ++i) {
+                if (!vok[i]) continue;
+                const float4 gv = reinterpret_cast<const float4*>(sg + us * g_tile + (vs + d.VS * i) * kFChunk)[lane];
+                float4 ga, gb;
+                bb_four<OP>(av, breg[i], gv, ga, gb);
+                dap = i == 0 ? ga : add4(dap, ga);
+                facc[i] = add4(facc[i], gb);
+            }
+        }
+        // da: the VS slots of each u, combined in a fixed tree
+        float* sc = scratch + (t & 1u) * kFSlots * kFChunk;
+        reinterpret_cast<float4*>(sc)[slot * kFLanes + lane] = dap;
+        if (vs == 0 && lane == 0) s_uao[t & 1u][us] = uao;
+        bool next_ok = ok;
+        if (threadIdx.x == 0 && ok && t + 1 < nsteps) {
+            next_ok = mbar_wait_bounded(&full[(t + 1) % kFStages], ((t + 1) / kFStages) & 1u, d.err);
+            if (next_ok) waited = t + 2;
+        }
+        ok = __syncthreads_and(next_ok) != 0;
+        // every thread is done with stage stg: refill it with step t + kFStages
+        if (threadIdx.x == 0 && ok && t + kFStages < nsteps) {
+            fence_proxy_async_smem();
+            issue(t + kFStages);
+        }
+        for (unsigned w = threadIdx.x; w < (d.US * kFChunk) << d.tp_log2; w += kFThreads) {
+            const unsigned o = w >> d.tp_log2, sub = w & (tp - 1);
+            const unsigned ou = o / kFChunk, ol = o % kFChunk;
+            const float* src = sc + ((ou << d.vs_log2) + sub * per) * kFChunk + ol;
+            float f = src[0];
+            for (unsigned x = 1; x < per; ++x) f += src[x * kFChunk];
+            double s = static_cast<double>(f);
+            for (unsigned m = 1; m < tp; m <<= 1) s += __shfl_xor_sync(0xffffffffu, s, m);
+            if (sub == 0 && u0 + ou + t * d.US < u1 && l0 + ol < d.L) {
+                const long long off = ka + s_uao[t & 1u][ou] + static_cast<long long>(l0 + ol);
+                if (d.da_d) d.da_d[off] = s;
+                else da[off] = static_cast<float>(s);
+            }
+        }
+        // db: flush the float blocks into the double accumulators
+        if ((t + 1) % kFFlush == 0 || t + 1 == nsteps) {
+#pragma unroll
+            for (unsigned i = 0; i < kFMaxNV; ++i) {
+                if (vok[i] && lane_ok) {
+                    double* p = dacc + (static_cast<unsigned long long>(us) * d.V + vs + d.VS * i) * kFChunk + lane * 4;
+                    p[0] += static_cast<double>(facc[i].x);
+                    p[1] += static_cast<double>(facc[i].y);
+                    p[2] += static_cast<double>(facc[i].z);
+                    p[3] += static_cast<double>(facc[i].w);
+                }
+                facc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+        // advance this slot's u by US (carry into U0)
+        c_c1 += d.US;
+        uao += static_cast<long long>(d.US) * d.ua1;
+        while (c_c1 >= d.U1) {
+            c_c1 -= d.U1;
+            uao += d.ua0 - static_cast<long long>(d.U1) * d.ua1;
+        }
+    }
+    // a wait that gave up may leave copies in flight: wait for them (bounded)
+    if (!ok && threadIdx.x == 0)
+        for (unsigned t = waited; t < issued; ++t) mbar_wait_bounded(&full[t % kFStages], (t / kFStages) & 1u, d.err);
+    __syncthreads();
+    // db: the US groups in order, then this segment's partial (or db itself)
+    for (unsigned o = threadIdx.x; o < d.V * kFChunk; o += kFThreads) {
+        const unsigned v = o / kFChunk, ol = o % kFChunk;
+        if (l0 + ol >= d.L) continue;
+        double s = 0.0;
+        for (unsigned x = 0; x < d.US; ++x) s += dacc[(static_cast<unsigned long long>(x) * d.V + v) * kFChunk + ol];
+        const long long off = kb + decode_vb(d, v) + static_cast<long long>(l0 + ol);
+        if (d.S > 1) partial[static_cast<unsigned long long>(seg) * d.db_count + off] = s;
+        else if (d.db_d) d.db_d[off] = s;
+        else db[off] = static_cast<float>(s);
+    }
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against libcuda); null when the driver does not provide it.
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// A float32 tiled tensor map; dims innermost first, strides in elements
+// (entries 1..rank-1 used). false when the driver rejects it.
+static bool encode_tensor_map(CUtensorMap* map, const float* base, int rank, const unsigned long long* dims,
+                              const long long* strides, const unsigned* box) {
+    auto fn = tensor_map_encoder();
+    if (!fn) return false;
+    cuuint64_t gdim[5], gstride[4];
+    cuuint32_t bdim[5], estride[5];
+    for (int i = 0; i < rank; ++i) {
+        gdim[i] = dims[i];
+        bdim[i] = box[i];
+        estride[i] = 1;
+        if (i > 0) {
+            if (strides[i] <= 0) return false;
+            gstride[i - 1] = static_cast<cuuint64_t>(strides[i]) * sizeof(float);
+        }
+    }
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, static_cast<cuuint32_t>(rank), const_cast<float*>(base), gdim,
+              gstride, bdim, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int OP>
+static void launch_fused(const CUtensorMap& gm, const CUtensorMap& am, const float* b, const FusedDesc& d,
+                         dim3 grid, std::size_t smem, float* da, float* db, double* partial) {
+    static bool configured = false;
+    if (!configured) {
+        VC_CUDA(cudaFuncSetAttribute(bcast_backward_fused<OP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(kFMaxSmem)));
+        configured = true;
+    }
+    bcast_backward_fused<OP><<<grid, kFThreads, smem, stream()>>>(gm, am, b, d, da, db, partial);
+}
+
+// Classify the output dims of a two-sided broadcast backward and launch
+// bcast_backward_fused when the shape fits it (see above; also g dense over
+// the output and every pointer 16-byte aligned). Returns false, having
+// launched nothing, otherwise.
+static bool try_fused_bcast_backward(int op, const float* a, const Src& sa, const float* b, const Src& sb,
+                                     const float* g, const Src& sg, const size_t* src, int rank, float* da,
+                                     float* db, double* da_d, double* db_d, std::size_t b_numel) {
+    if (!(da || da_d) || !(db || db_d)) return false;
+    long long contiguous = 1;
+    for (int i = rank - 1; i >= 0; --i) {
+        if (src[i] != 1 && sg.st[i] != contiguous) return false;
+        contiguous *= static_cast<long long>(src[i]);
+    }
+    // classes: 1 = both span (kept by both), 2 = only a spans (U), 3 = only b spans (V)
+    struct Dim { int cls; unsigned long long size; long long st[3]; };  // g, a, b strides
+    Dim dims[kMaxRank];
+    int nd = 0;
+    for (int i = 0; i < rank; ++i) {
+        if (src[i] == 1) continue;
+        const bool in_a = sa.st[i] != 0, in_b = sb.st[i] != 0;
+        if (!in_a && !in_b) return false;
+        Dim cur{in_a && in_b ? 1 : (in_a ? 2 : 3), src[i], {sg.st[i], sa.st[i], sb.st[i]}};
+        if (nd > 0 && dims[nd - 1].cls == cur.cls) {
+            Dim& prev = dims[nd - 1];
+            bool ok = true;
+            for (int k = 0; k < 3; ++k) ok = ok && prev.st[k] == cur.st[k] * static_cast<long long>(cur.size);
+            if (ok) {
+                prev.size *= cur.size;
+                for (int k = 0; k < 3; ++k) prev.st[k] = cur.st[k];
+                continue;
+            }
+        }
+        dims[nd++] = cur;
+    }
+    if (nd < 3 || dims[nd - 1].cls != 1) return false;
+    FusedDesc d{};
+    d.L = dims[nd - 1].size;
+    if (d.L % 4 != 0 || d.L > 0x7fffffffull) return false;
+    const void* ptrs[5] = {a, b, g, da ? static_cast<const void*>(da) : da_d, db ? static_cast<const void*>(db) : db_d};
+    for (int k = 0; k < 5; ++k)
+        if (!aligned16(ptrs[k])) return false;
+    Dim ud[2], vd[2], kd[2];  // outer first
+    int nu = 0, nv = 0, nk = 0;
+    for (int i = 0; i + 1 < nd; ++i) {
+        const Dim& x = dims[i];
+        if (x.size > 0x7fffffffull) return false;
+        if (x.cls == 2) { if (nu == 2) return false; ud[nu++] = x; }
+        else if (x.cls == 3) { if (nv == 2) return false; vd[nv++] = x; }
+        else { if (nk == 2) return false; kd[nk++] = x; }
+    }
+    if (nu == 0 || nv == 0) return false;
+    unsigned long long U = 1, V = 1, K = 1;
+    for (int i = 0; i < nu; ++i) U *= ud[i].size;
+    for (int i = 0; i < nv; ++i) V *= vd[i].size;
+    for (int i = 0; i < nk; ++i) K *= kd[i].size;
+    if (V < 2 || V > kFMaxV || U < 2 || U > 0x7fffffffull || K > 65535) return false;
+    d.U = static_cast<unsigned>(U);
+    d.V = static_cast<unsigned>(V);
+    d.nv = nv;
+    for (int i = 0; i < nv; ++i) { d.vdims[i] = static_cast<unsigned>(vd[i].size); d.vb[i] = vd[i].st[2]; }
+    d.nk = nk;
+    for (int i = 0; i < nk; ++i) { d.kdims[i] = kd[i].size; d.ka[i] = kd[i].st[1]; d.kb[i] = kd[i].st[2]; }
+    // U as (U0 outer, U1 inner); one U dim is (1, U)
+    const Dim uinner = ud[nu - 1];
+    d.has_u0 = nu == 2;
+    d.U1 = static_cast<unsigned>(uinner.size);
+    d.U0 = nu == 2 ? static_cast<unsigned>(ud[0].size) : 1u;
+    d.u1fd = FastDiv(d.U1);
+    d.ua1 = uinner.st[1];
+    d.ua0 = nu == 2 ? ud[0].st[1] : 0;
+    // tensor maps, dims innermost first. g: (L, V dims, U1, [U0], K dims);
+    // a: (L, U1, [U0], K dims). Boxes: 32 floats x all of V; 32 floats.
+    unsigned long long gdims[5], adims[5];
+    long long gstr[5], astr[5];
+    unsigned gbox[5], abox[5];
+    int rg = 0, ra = 0;
+    gdims[rg] = d.L; gstr[rg] = 1; gbox[rg++] = kFChunk;
+    for (int i = nv - 1; i >= 0; --i) {
+        gdims[rg] = vd[i].size; gstr[rg] = vd[i].st[0]; gbox[rg++] = static_cast<unsigned>(vd[i].size);
+    }
+    adims[ra] = d.L; astr[ra] = 1; abox[ra++] = kFChunk;
+    d.ucoord_g = rg;
+    d.ucoord_a = ra;
+    gdims[rg] = uinner.size; gstr[rg] = uinner.st[0]; gbox[rg++] = 1;
+    adims[ra] = uinner.size; astr[ra] = uinner.st[1]; abox[ra++] = 1;
+    if (nu == 2) {
+        gdims[rg] = ud[0].size; gstr[rg] = ud[0].st[0]; gbox[rg++] = 1;
+        adims[ra] = ud[0].size; astr[ra] = ud[0].st[1]; abox[ra++] = 1;
+    }
+    for (int i = nk - 1; i >= 0; --i) {
+        if (rg == 5 || ra == 5) return false;
+        gdims[rg] = kd[i].size; gstr[rg] = kd[i].st[0]; gbox[rg++] = 1;
+        adims[ra] = kd[i].size; astr[ra] = kd[i].st[1]; abox[ra++] = 1;
+    }
+    d.rank_g = rg;
+    d.rank_a = ra;
+    CUtensorMap gm{}, am{};
+    if (!encode_tensor_map(&gm, g, rg, gdims, gstr, gbox)) return false;
+    if (!encode_tensor_map(&am, a, ra, adims, astr, abox)) return false;
+    unsigned vs = 1;
+    while (vs * 2 <= V && vs * 2 <= kFSlots) vs *= 2;
+    d.VS = vs;
+    d.US = kFSlots / vs;
+    d.NV = static_cast<unsigned>((V + vs - 1) / vs);
+    const unsigned tp = std::max(1u, std::min(vs, kFThreads / (d.US * kFChunk)));
+    d.vs_log2 = 0;
+    while ((1u << d.vs_log2) < vs) ++d.vs_log2;
+    d.tp_log2 = 0;
+    while ((1u << d.tp_log2) < tp) ++d.tp_log2;
+    d.stage_bytes = d.US * (d.V + 1) * kFChunk * static_cast<unsigned>(sizeof(float));
+    const unsigned long long chunks = (d.L + kFChunk - 1) / kFChunk;
+    unsigned long long S = (kFTargetCtas + chunks * K - 1) / (chunks * K);
+    S = std::min<unsigned long long>(S, (U + kFMinUSeg - 1) / kFMinUSeg);
+    S = std::max<unsigned long long>(1, std::min<unsigned long long>(S, 65535));
+    unsigned long long useg = (U + S - 1) / S;
+    useg = (useg + d.US - 1) / d.US * d.US;
+    d.useg = static_cast<unsigned>(useg);
+    d.S = static_cast<unsigned>((U + useg - 1) / useg);
+    d.db_count = b_numel;
+    d.da_d = da_d;
+    d.db_d = db_d;
+    d.err = device_error_word();
+    const std::size_t smem = kFStages * static_cast<std::size_t>(d.stage_bytes) +
+                             static_cast<std::size_t>(d.US) * d.V * kFChunk * sizeof(double) +
+                             2 * kFSlots * kFChunk * sizeof(float);
+    if (smem > kFMaxSmem) return false;
+    Scratch partial(d.S > 1 ? static_cast<std::size_t>(d.S) * b_numel * sizeof(double) : 8);
+    const dim3 grid(static_cast<unsigned>(chunks), d.S, static_cast<unsigned>(K));
+    switch (op) {
+        case VC_ADD: launch_fused<VC_ADD>(gm, am, b, d, grid, smem, da, db, partial.as<double>()); break;
+        case VC_SUB: launch_fused<VC_SUB>(gm, am, b, d, grid, smem, da, db, partial.as<double>()); break;
+        case VC_MUL: launch_fused<VC_MUL>(gm, am, b, d, grid, smem, da, db, partial.as<double>()); break;
+        default: launch_fused<VC_DIV>(gm, am, b, d, grid, smem, da, db, partial.as<double>()); break;
+    }
+    check_launch("bcast_backward_fused");
+    if (d.S > 1) {
+        reduce_col_finish<<<grid_for(b_numel, kThreads), kThreads, 0, stream()>>>(partial.as<double>(), d.S, b_numel,
+                                                                                   0.0f, db, db_d);
+        check_launch("bcast_backward_finish");
+    }
+    return true;
+}
+
+// ---------------------------------------------------------------------------
 // Max / argmax over [outer, length, inner] with the reference's scan
 // semantics (cpu_backend.cpp:443-453): a strictly larger value replaces the
 // best, so the first maximal index wins; NaN never replaces, so a NaN wins
@@ -986,6 +1483,9 @@ vc_status vc_cuda_binary_backward(int op, const float* a, const size_t* a_shape,
         check_launch("binary_backward_flat");
         return VC_OK;
     }
+    if (da && db && try_fused_bcast_backward(op, a, sa, b, sb, g, sg, src, rank, da, db, nullptr, nullptr,
+                                             checked_numel(b_shape, b_rank)))
+        return VC_OK;
     if (da) {
         Src ops[3] = {sg, sb, sb};
         const int f = (op == VC_ADD || op == VC_SUB) ? V_G : (op == VC_MUL ? V_MUL : V_DIV_A);
@@ -1149,6 +1649,10 @@ vc_status vc_cuda_binary_backward_partial(int op, const float* a, const size_t* 
     const Src sg = align(g, g_shape, g_rank, src, rank, "binary_backward_partial");
     const Src sa = align(a, a_shape, a_rank, src, rank, "binary_backward_partial");
     const Src sb = align(b, b_shape, b_rank, src, rank, "binary_backward_partial");
+    if (da_partial && db_partial &&
+        try_fused_bcast_backward(op, a, sa, b, sb, g, sg, src, rank, nullptr, nullptr, da_partial, db_partial,
+                                 checked_numel(b_shape, b_rank)))
+        return VC_OK;
     if (da_partial) {
         Src ops[3] = {sg, sb, sb};
         const int f = (op == VC_ADD || op == VC_SUB) ? V_G : (op == VC_MUL ? V_MUL : V_DIV_A);

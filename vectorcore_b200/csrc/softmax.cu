@@ -18,7 +18,7 @@
 //
 // The arithmetic is the reference's, operation by operation:
 //   m  = max(x) with the scan semantics of cpu::reduce_axis,
-//   s  = float(double sum of expf(x - m)),  l = logf(s),
+//   s  = float(sum of exp(x - m)),  l = logf(s),
 //   log_softmax = (x - m) - l,  softmax = expf(log_softmax),
 // and the backward passes replay the reference autograd chain (engine order
 // of src/tensor.cpp:266-300) from the saved m and s:
@@ -26,14 +26,21 @@
 //   softmax:     gy = g * y;  dx = gy + ((float(sum(-gy)) / s) + 0) * expf(x - m)
 //   cross-entropy (upstream u, batch B): dp = (-(u / B)) + 0,
 //     dx = dp * onehot + ((dl / s) + 0) * expf(x - m) with dl = sum(-dp*onehot).
-// Results therefore differ from the CPU path only through expf/logf ulps and
-// the order of double additions.
+// The reference sums in double. Here the staged (TMA) paths add each group of
+// four terms in float and the group sums in double, and the exp terms of s
+// come from exp_sum_term (ex2-based, a few ulps) rather than expf; every
+// per-element output still uses expf. Results therefore differ from the CPU
+// path only through exp/log ulps and the order and grouping of the additions,
+// all far inside the 1e-5 sum tolerance.
 #include "vc_internal.cuh"
 
 #include <cooperative_groups.h>
 
 #include <algorithm>
 #include <cmath>
+#include <map>
+#include <mutex>
+#include <utility>
 
 namespace cg = cooperative_groups;
 
@@ -44,47 +51,16 @@ namespace {
 constexpr unsigned kThreads = 256;
 constexpr unsigned kSliceTarget = 8192;     // floats per CTA slice (32 KB)
 constexpr unsigned kSliceMax = 24576;       // floats per CTA slice at cluster size 8 (96 KB)
-constexpr long long kWaitSpins = 1ll << 24; // bounded mbarrier wait (iterations)
 
 enum Mode { LSM_FWD = 0, SM_FWD = 1, CE_FWD = 2, LSM_BWD = 3, SM_BWD = 4 };
 
-// ---- TMA bulk copy + mbarrier helpers --------------------------------------
-__device__ __forceinline__ unsigned smem_addr(const void* p) {
-    return static_cast<unsigned>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void mbar_init(unsigned long long* bar, unsigned count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_fence_init() {
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(unsigned long long* bar, unsigned bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
-                 : "memory");
-}
+// ---- bulk copy into this CTA's shared memory (mbarrier helpers: vc_internal.cuh)
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, unsigned bytes, unsigned long long* bar) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
             smem_addr(dst)),
         "l"(src), "r"(bytes), "r"(smem_addr(bar))
         : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned parity) {
-    unsigned ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(smem_addr(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// Wait for phase `parity` with an iteration limit; false (and the device
-// error bit) when it gave up.
-__device__ __forceinline__ bool mbar_wait_bounded(unsigned long long* bar, unsigned parity, unsigned* err) {
-    for (long long i = 0; i < kWaitSpins; ++i)
-        if (mbar_try_wait(bar, parity)) return true;
-    atomicOr(err, kErrWaitTimeout);
-    return false;
 }
 
 struct RowArgs {
@@ -100,6 +76,40 @@ struct RowArgs {
     unsigned seg;      // floats per CTA slice (multiple of 4)
     unsigned* err;
 };
+
+// ---- row-sum helpers ----------------------------------------------------------
+// exp(x) for the terms of a row sum (x = logit - row max <= 0): 2^(x log2 e)
+// on the SFU's ex2.approx, with the product x * log2(e) carried in two
+// floats -- t = fl(x * L2E_HI), tl = (x * L2E_HI - t) + x * L2E_LO via FMA
+// (Dekker-style product splitting) -- and 2^tl applied to first order,
+// 2^t * (1 + tl ln 2). The error is ex2.approx's (relative below 2^-22) plus
+// about 1e-7 from the first-order step: a few float ulps of each term, far
+// inside the sum tolerance. Per-element outputs keep expf. x is clamped
+// (NaN-preserving) at -110, where 2^t is already 0.
+constexpr float kL2eHi = 0x1.715476p+0f;   // log2(e) rounded to float
+constexpr float kL2eLo = 0x1.4ae0c0p-26f;  // log2(e) - kL2eHi
+constexpr float kLn2 = 0x1.62e430p-1f;     // ln(2) rounded to float
+__device__ __forceinline__ float exp_sum_term(float x) {
+    float xc;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(xc) : "f"(x), "f"(-110.0f));
+    const float t = xc * kL2eHi;
+    const float tl = __fmaf_rn(xc, kL2eLo, __fmaf_rn(xc, kL2eHi, -t));
+    float e;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(t));
+    return __fmaf_rn(e, tl * kLn2, e);
+}
+
+// Row sums accumulate per float4: the four terms in float ((x + y) + (z + w)),
+// that partial in double -- one float->double conversion per four elements
+// rather than per element (the conversion pipe runs at 16/clk/SM and the
+// SFU's ex2 shares it). A float partial that is not finite (overflow of large
+// upstream gradients) is replaced by the four terms added in double, so an
+// infinity appears only where the double sum has one.
+__device__ __forceinline__ double quad_sum(float4 v) {
+    const float q = (v.x + v.y) + (v.z + v.w);
+    if (isfinite(q)) return static_cast<double>(q);
+    return ((static_cast<double>(v.x) + static_cast<double>(v.y)) + static_cast<double>(v.z)) + static_cast<double>(v.w);
+}
 
 // ---- block / cluster combines (fixed order: the same result in every CTA) ----
 __device__ __forceinline__ float block_fmax(float v, float* scratch) {
@@ -240,8 +250,8 @@ row_kernel(const RowArgs a, unsigned long long row0) {
         if constexpr (BULK) {
             for (unsigned j = threadIdx.x; j < n4; j += kThreads) {
                 const float4 v = ld_smem4(sx, j);
-                acc0 += static_cast<double>(expf(v.x - m)) + static_cast<double>(expf(v.y - m));
-                acc1 += static_cast<double>(expf(v.z - m)) + static_cast<double>(expf(v.w - m));
+                acc0 += quad_sum(make_float4(exp_sum_term(v.x - m), exp_sum_term(v.y - m), exp_sum_term(v.z - m),
+                                             exp_sum_term(v.w - m)));
             }
         } else {
             for (unsigned k = threadIdx.x; k < n; k += kThreads) acc0 += static_cast<double>(expf(sx[k] - m));
@@ -283,8 +293,7 @@ row_kernel(const RowArgs a, unsigned long long row0) {
             if constexpr (BULK) {
                 for (unsigned j = threadIdx.x; j < n4; j += kThreads) {
                     const float4 g = ld_smem4(sg, j);
-                    acc0 += static_cast<double>(-g.x) + static_cast<double>(-g.y);
-                    acc1 += static_cast<double>(-g.z) + static_cast<double>(-g.w);
+                    acc0 += quad_sum(make_float4(-g.x, -g.y, -g.z, -g.w));
                 }
             } else {
                 for (unsigned k = threadIdx.x; k < n; k += kThreads) acc0 += static_cast<double>(-sg[k]);
@@ -310,8 +319,7 @@ row_kernel(const RowArgs a, unsigned long long row0) {
                     const float4 x = ld_smem4(sx, j), g = ld_smem4(sg, j);
                     const float4 gy = make_float4(gy_of(x.x, g.x), gy_of(x.y, g.y), gy_of(x.z, g.z), gy_of(x.w, g.w));
                     reinterpret_cast<float4*>(sg)[j] = gy;
-                    acc0 += static_cast<double>(-gy.x) + static_cast<double>(-gy.y);
-                    acc1 += static_cast<double>(-gy.z) + static_cast<double>(-gy.w);
+                    acc0 += quad_sum(make_float4(-gy.x, -gy.y, -gy.z, -gy.w));
                 }
             } else {
                 for (unsigned k = threadIdx.x; k < n; k += kThreads) {
@@ -459,6 +467,273 @@ ce_backward_kernel(const float* __restrict__ x, const long long* __restrict__ ta
     }
 }
 
+// ---------------------------------------------------------------------------
+// Pipelined row kernel for 16-byte-aligned rows whose length is a multiple
+// of 4: a persistent grid of clusters, cluster k handling rows k,
+// k + clusters, ... Each CTA double-buffers its slice of the row in shared
+// memory ([x slice][g slice] per stage; x in every mode, g in the backward
+// ones): the bulk copy of the next row's slice is issued when the current
+// row starts, so the copy engine streams HBM while the CTA computes.
+//
+// Waiting: only thread 0 polls an mbarrier (stage copies and exchanges);
+// __syncthreads_and then releases the CTA and shares whether the wait
+// succeeded, so no warp spins on shared memory.
+//
+// Cluster exchange without cluster barriers: every warp pushes its partial
+// into slot [rank * kWarps + warp] of EVERY CTA of the cluster with st.async,
+// whose completion is counted in bytes on the receiving CTA's mbarrier; each
+// CTA then folds its C * kWarps slots lane-parallel with a fixed xor tree (the
+// same result in every CTA). No release fence is involved (a cluster
+// barrier's would wait for all of the thread's global stores in flight).
+// Slots and mbarriers are double-buffered by row parity: a CTA can run at
+// most one exchange ahead of a peer, since it needs that peer's contribution
+// to finish the previous one.
+// ---------------------------------------------------------------------------
+constexpr unsigned kWarps = kThreads / 32;
+constexpr unsigned kMaxCluster = 8;
+constexpr unsigned kStageFloats = 8192;     // floats per stage (x and g together)
+constexpr unsigned kStageFloatsMax = 24576; // ... at cluster size 8 (96 KB a stage, two stages)
+
+template <int MODE> struct PipeTraits {
+    static constexpr bool FWD = MODE == LSM_FWD || MODE == SM_FWD || MODE == CE_FWD;
+    static constexpr bool STAGE_G = MODE == LSM_BWD || MODE == SM_BWD;
+    static constexpr unsigned NBUF = STAGE_G ? 2u : 1u;
+};
+
+__device__ __forceinline__ float warp_fmax(float v) {
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, m));
+    return v;
+}
+__device__ __forceinline__ unsigned long long warp_umin(unsigned long long v) {
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, m));
+    return v;
+}
+__device__ __forceinline__ unsigned mapa_cluster(unsigned cta_addr, unsigned rank) {
+    unsigned r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(cta_addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void st_async_b32(unsigned addr, unsigned v, unsigned bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(addr), "r"(v),
+                 "r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ void st_async_b64(unsigned addr, unsigned long long v, unsigned bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b64 [%0], %1, [%2];" ::"r"(addr), "l"(v),
+                 "r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ unsigned long long bits64(double v) { return static_cast<unsigned long long>(__double_as_longlong(v)); }
+__device__ __forceinline__ unsigned long long bits64(unsigned long long v) { return v; }
+
+// Push this warp's value (lane 0's) to every CTA of the cluster, then wait
+// (thread 0, bounded) for all C * kWarps values of this exchange to land in
+// this CTA's `slots`. Returns the CTA-uniform success flag. When an earlier
+// wait failed (ok false) the values are still sent, so no peer is left
+// waiting, but nobody waits here.
+template <class T>
+__device__ __forceinline__ bool exchange(T v, T* slots, unsigned long long* bar, unsigned parity, unsigned C,
+                                         unsigned rank, bool ok, unsigned* err) {
+    if (threadIdx.x == 0) mbar_expect_tx(bar, C * kWarps * static_cast<unsigned>(sizeof(T)));
+    if ((threadIdx.x & 31) == 0) {
+        const unsigned slot = smem_addr(slots + rank * kWarps + (threadIdx.x >> 5));
+        const unsigned b = smem_addr(bar);
+        for (unsigned r = 0; r < C; ++r) {
+            if constexpr (sizeof(T) == 4) st_async_b32(mapa_cluster(slot, r), __float_as_uint(v), mapa_cluster(b, r));
+            else st_async_b64(mapa_cluster(slot, r), bits64(v), mapa_cluster(b, r));
+        }
+    }
+    bool good = ok;
+    if (threadIdx.x == 0 && ok) good = mbar_wait_bounded(bar, parity, err);
+    return __syncthreads_and(good) != 0;
+}
+
+__device__ __forceinline__ float fold_fmax(const float* slots, unsigned C) {
+    float t = -INFINITY;
+    for (unsigned i = threadIdx.x & 31; i < C * kWarps; i += 32) t = fmaxf(t, slots[i]);
+    return warp_fmax(t);
+}
+__device__ __forceinline__ unsigned long long fold_umin(const unsigned long long* slots, unsigned C) {
+    unsigned long long t = ~0ull;
+    for (unsigned i = threadIdx.x & 31; i < C * kWarps; i += 32) t = min(t, slots[i]);
+    return warp_umin(t);
+}
+__device__ __forceinline__ double fold_sum(const double* slots, unsigned C) {
+    double t = 0.0;
+    for (unsigned i = threadIdx.x & 31; i < C * kWarps; i += 32) t += slots[i];
+    return warp_sum(t);
+}
+__device__ __forceinline__ float4 neg4(float4 v) { return make_float4(-v.x, -v.y, -v.z, -v.w); }
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads)
+row_pipe_kernel(const RowArgs a) {
+    using T = PipeTraits<MODE>;
+    extern __shared__ __align__(128) float smem[];
+    __shared__ unsigned long long bar[2];        // stage copies
+    __shared__ unsigned long long xbar[3][2];    // exchanges: max, first-zero index, sum
+    __shared__ float xs_max[2][kMaxCluster * kWarps];
+    __shared__ unsigned long long xs_idx[2][kMaxCluster * kWarps];
+    __shared__ double xs_sum[2][kMaxCluster * kWarps];
+
+    cg::cluster_group cluster = cg::this_cluster();
+    const unsigned C = cluster.num_blocks();
+    const unsigned rank = cluster.block_rank();
+    const unsigned long long nclusters = gridDim.x / C;
+    const unsigned long long cid = blockIdx.x / C;
+    const unsigned long long c0 = static_cast<unsigned long long>(rank) * a.seg;
+    const unsigned n = c0 < a.L ? static_cast<unsigned>(min(static_cast<unsigned long long>(a.seg), a.L - c0)) : 0u;
+    const unsigned n4 = n / 4;
+    const unsigned stage_floats = a.seg * T::NBUF;
+    const unsigned bytes = n * 4u * T::NBUF;
+
+    if (threadIdx.x == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        for (int k = 0; k < 3; ++k) {
+            mbar_init(&xbar[k][0], 1);
+            mbar_init(&xbar[k][1], 1);
+        }
+        mbar_fence_init();
+    }
+    // every CTA's mbarriers are initialised before any peer signals them
+    cluster.sync();
+    unsigned loads[2] = {0, 0}, seen[2] = {0, 0};  // thread 0: copies issued / completed per stage
+    auto issue = [&](unsigned st, unsigned long long row) {
+        float* base = smem + st * stage_floats;
+        mbar_expect_tx(&bar[st], bytes);
+        bulk_load(base, a.x + row * a.L + c0, n * 4u, &bar[st]);
+        if (T::STAGE_G) bulk_load(base + a.seg, a.g + row * a.L + c0, n * 4u, &bar[st]);
+        ++loads[st];
+    };
+    if (threadIdx.x == 0 && bytes && cid < a.rows) issue(0, cid);
+
+    bool ok = true;                   // CTA-uniform: every wait so far completed
+    unsigned it = 0, nz = 0;          // rows done; first-zero exchanges done
+    for (unsigned long long row = cid; row < a.rows; row += nclusters, ++it) {
+        const unsigned st = it & 1u, par = (it >> 1) & 1u;
+        float m_saved = 0.0f, s_saved = 0.0f;
+        if constexpr (!T::FWD) {
+            m_saved = __ldg(a.row_max + row);
+            s_saved = __ldg(a.row_sum + row);
+        }
+        bool good = ok;
+        if (threadIdx.x == 0 && ok && bytes) {
+            good = mbar_wait_bounded(&bar[st], par, a.err);
+            if (good) ++seen[st];
+        }
+        // publishes the stage; every thread is also done with the other stage
+        // (the previous row), which is refilled with the next row right away
+        ok = __syncthreads_and(good) != 0;
+        if (threadIdx.x == 0 && ok && bytes && row + nclusters < a.rows) {
+            fence_proxy_async_smem();
+            issue(st ^ 1u, row + nclusters);
+        }
+        float* sx = smem + st * stage_floats;
+        float* sg = sx + a.seg;
+        float* yrow = a.y ? a.y + row * a.L + c0 : nullptr;
+
+        if constexpr (T::FWD) {
+            const float first = __ldg(a.x + row * a.L);
+            // ---- row max m: fmaxf skips NaN; then the scan's exact rules ----
+            float mloc = -INFINITY;
+            for (unsigned j = threadIdx.x; j < n4; j += kThreads) {
+                const float4 v = ld_smem4(sx, j);
+                mloc = fmaxf(mloc, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
+            }
+            ok = exchange(warp_fmax(mloc), xs_max[st], &xbar[0][st], par, C, rank, ok, a.err);
+            float m = fold_fmax(xs_max[st], C);
+            if (first != first) {
+                m = first;  // the scan never leaves a NaN at index 0
+            } else if (m == 0.0f) {
+                // a zero maximum is the FIRST zero of the row (its sign
+                // matters); the condition is the same in every CTA
+                unsigned long long idx = ~0ull;
+                for (unsigned k = threadIdx.x; k < n; k += kThreads)
+                    if (sx[k] == 0.0f) { idx = c0 + k; break; }
+                const unsigned zb = nz & 1u;
+                ok = exchange(warp_umin(idx), xs_idx[zb], &xbar[1][zb], (nz >> 1) & 1u, C, rank, ok, a.err);
+                idx = fold_umin(xs_idx[zb], C);
+                ++nz;
+                if (idx < a.L) m = __ldg(a.x + row * a.L + idx);
+            }
+            // ---- s = float(sum of exp(x - m)) ----
+            double part = 0.0;
+            for (unsigned j = threadIdx.x; j < n4; j += kThreads) {
+                const float4 v = ld_smem4(sx, j);
+                part += quad_sum(make_float4(exp_sum_term(v.x - m), exp_sum_term(v.y - m), exp_sum_term(v.z - m),
+                                             exp_sum_term(v.w - m)));
+            }
+            ok = exchange(warp_sum(part), xs_sum[st], &xbar[2][st], par, C, rank, ok, a.err);
+            const float s = static_cast<float>(fold_sum(xs_sum[st], C));
+            const float l = logf(s);
+            if (rank == 0 && threadIdx.x == 0) {
+                if (a.row_max) a.row_max[row] = m;
+                if (a.row_sum) a.row_sum[row] = s;
+            }
+            if constexpr (MODE == CE_FWD) {
+                const long long t = __ldg(a.targets + row);
+                if (t < 0 || static_cast<unsigned long long>(t) >= a.L) {
+                    if (rank == 0 && threadIdx.x == 0) { atomicOr(a.err, kErrBadTarget); a.row_term[row] = 0.0f; }
+                } else if (threadIdx.x == 0 && static_cast<unsigned long long>(t) >= c0 &&
+                           static_cast<unsigned long long>(t) < c0 + n) {
+                    a.row_term[row] = (sx[t - c0] - m) - l;
+                }
+            } else {
+                auto f = [&](float v) {
+                    const float ls = (v - m) - l;
+                    return MODE == SM_FWD ? expf(ls) : ls;
+                };
+                for (unsigned j = threadIdx.x; j < n4; j += kThreads) {
+                    const float4 v = ld_smem4(sx, j);
+                    st4_stream(yrow + 4 * j, make_float4(f(v.x), f(v.y), f(v.z), f(v.w)));
+                }
+            }
+        } else if constexpr (MODE == LSM_BWD) {
+            // dx = g + ((float(sum(-g)) / s) + 0) * expf(x - m)
+            const float m = m_saved, s = s_saved;
+            double part = 0.0;
+            for (unsigned j = threadIdx.x; j < n4; j += kThreads) part += quad_sum(neg4(ld_smem4(sg, j)));
+            ok = exchange(warp_sum(part), xs_sum[st], &xbar[2][st], par, C, rank, ok, a.err);
+            const float dl = static_cast<float>(fold_sum(xs_sum[st], C));
+            const float de = (dl / s) + 0.0f;
+            for (unsigned j = threadIdx.x; j < n4; j += kThreads) {
+                const float4 g = ld_smem4(sg, j), x = ld_smem4(sx, j);
+                st4_stream(yrow + 4 * j, make_float4(g.x + de * expf(x.x - m), g.y + de * expf(x.y - m),
+                                                     g.z + de * expf(x.z - m), g.w + de * expf(x.w - m)));
+            }
+        } else {  // SM_BWD: gy = g * y; dx = gy + ((float(sum(-gy)) / s) + 0) * expf(x - m)
+            const float m = m_saved, s = s_saved;
+            const float l = logf(s);
+            auto gy_of = [&](float x, float g) { return g * expf((x - m) - l); };
+            double part = 0.0;
+            for (unsigned j = threadIdx.x; j < n4; j += kThreads) {
+                const float4 x = ld_smem4(sx, j), g = ld_smem4(sg, j);
+                const float4 gy = make_float4(gy_of(x.x, g.x), gy_of(x.y, g.y), gy_of(x.z, g.z), gy_of(x.w, g.w));
+                reinterpret_cast<float4*>(sg)[j] = gy;
+                part += quad_sum(neg4(gy));
+            }
+            ok = exchange(warp_sum(part), xs_sum[st], &xbar[2][st], par, C, rank, ok, a.err);
+            const float dl = static_cast<float>(fold_sum(xs_sum[st], C));
+            const float de = (dl / s) + 0.0f;
+            for (unsigned j = threadIdx.x; j < n4; j += kThreads) {
+                const float4 x = ld_smem4(sx, j), gy = ld_smem4(sg, j);
+                st4_stream(yrow + 4 * j, make_float4(gy.x + de * expf(x.x - m), gy.y + de * expf(x.y - m),
+                                                     gy.z + de * expf(x.z - m), gy.w + de * expf(x.w - m)));
+            }
+        }
+    }
+    // Only a wait that gave up can leave a copy in flight: wait (bounded)
+    // for every copy issued but not seen complete before the memory goes.
+    if (!ok && threadIdx.x == 0)
+        for (unsigned s2 = 0; s2 < 2; ++s2)
+            for (unsigned k = seen[s2]; k < loads[s2]; ++k) mbar_wait_bounded(&bar[s2], k & 1u, a.err);
+    // No CTA leaves while a peer may still signal or write its shared memory.
+    cluster.sync();
+}
+
 template <int MODE, bool BULK>
 static void launch_rows_mode(const RowArgs& a, unsigned C, std::size_t smem) {
     static bool configured = false;
@@ -487,24 +762,88 @@ static void launch_rows_mode(const RowArgs& a, unsigned C, std::size_t smem) {
     check_launch("softmax_rows");
 }
 
+static cudaLaunchConfig_t cluster_config(unsigned long long ctas, unsigned C, std::size_t smem,
+                                         cudaLaunchAttribute* attr) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(ctas), 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream();
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = C;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cfg;
+}
+
+// Persistent grid size: the clusters of (C, smem) the device holds at once,
+// queried once per configuration.
+template <int MODE>
+static unsigned long long resident_clusters(unsigned C, std::size_t smem) {
+    static std::mutex mu;
+    static std::map<std::pair<unsigned, std::size_t>, int> cache;
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find({C, smem});
+    if (it != cache.end()) return static_cast<unsigned long long>(it->second);
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = cluster_config(static_cast<unsigned long long>(C) * sm_count(), C, smem, attr);
+    int n = 0;
+    VC_CUDA(cudaOccupancyMaxActiveClusters(&n, row_pipe_kernel<MODE>, &cfg));
+    if (n < 1) fail(VC_ERR_RUNTIME, "softmax: no cluster of this shape fits on the device");
+    cache[{C, smem}] = n;
+    return static_cast<unsigned long long>(n);
+}
+
+template <int MODE>
+static void launch_rows_pipelined(const RowArgs& a, unsigned C, std::size_t smem) {
+    static bool configured = false;
+    if (!configured) {
+        VC_CUDA(cudaFuncSetAttribute(row_pipe_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        VC_CUDA(cudaFuncSetAttribute(row_pipe_kernel<MODE>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+        configured = true;
+    }
+    const unsigned long long clusters = std::min<unsigned long long>(a.rows, resident_clusters<MODE>(C, smem));
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = cluster_config(clusters * C, C, smem, attr);
+    VC_CUDA(cudaLaunchKernelEx(&cfg, row_pipe_kernel<MODE>, a));
+    check_launch("softmax_rows_pipelined");
+}
+
 template <int MODE>
 static void launch_family(RowArgs a, std::size_t outer, std::size_t length, std::size_t inner) {
     constexpr bool STAGE_X = MODE == LSM_FWD || MODE == SM_FWD || MODE == CE_FWD || MODE == SM_BWD;
     constexpr bool STAGE_G = MODE == LSM_BWD || MODE == SM_BWD;
     a.err = device_error_word();
     a.L = length;
-    if (inner == 1 && length <= 8ull * kSliceMax) {
-        unsigned C = 1;
-        while (C < 8 && (length + C - 1) / C > kSliceTarget) C <<= 1;
-        unsigned long long seg = (length + C - 1) / C;
-        seg = (seg + 3) / 4 * 4;
-        a.seg = static_cast<unsigned>(seg);
+    if (inner == 1) {
         a.rows = outer;
-        const std::size_t smem = seg * sizeof(float) * ((STAGE_X ? 1 : 0) + (STAGE_G ? 1 : 0));
-        const bool bulk = length % 4 == 0 && (!STAGE_X || aligned16(a.x)) && (!STAGE_G || aligned16(a.g));
-        if (bulk) launch_rows_mode<MODE, true>(a, C, smem);
-        else launch_rows_mode<MODE, false>(a, C, smem);
-        return;
+        const bool aligned = length % 4 == 0 && aligned16(a.x) && (!STAGE_G || aligned16(a.g)) &&
+                             (!a.y || aligned16(a.y));
+        if (aligned) {
+            constexpr unsigned NB = PipeTraits<MODE>::NBUF;
+            unsigned C = 1;
+            while (C < 8 && (length + C - 1) / C > kStageFloats / NB) C <<= 1;
+            const unsigned long long seg = ((length + C - 1) / C + 3) / 4 * 4;
+            if (seg * NB <= kStageFloatsMax) {
+                a.seg = static_cast<unsigned>(seg);
+                launch_rows_pipelined<MODE>(a, C, 2 * seg * NB * sizeof(float));
+                return;
+            }
+        }
+        if (length <= 8ull * kSliceMax) {
+            unsigned C = 1;
+            while (C < 8 && (length + C - 1) / C > kSliceTarget) C <<= 1;
+            unsigned long long seg = (length + C - 1) / C;
+            seg = (seg + 3) / 4 * 4;
+            a.seg = static_cast<unsigned>(seg);
+            const std::size_t smem = seg * sizeof(float) * ((STAGE_X ? 1 : 0) + (STAGE_G ? 1 : 0));
+            const bool bulk = length % 4 == 0 && (!STAGE_X || aligned16(a.x)) && (!STAGE_G || aligned16(a.g));
+            if (bulk) launch_rows_mode<MODE, true>(a, C, smem);
+            else launch_rows_mode<MODE, false>(a, C, smem);
+            return;
+        }
     }
     a.rows = outer * inner;
     col_kernel<MODE><<<grid_for(outer * inner, kThreads), kThreads, 0, stream()>>>(a, outer, inner);

@@ -122,6 +122,50 @@ __device__ __forceinline__ void st4(float* p, float4 v) { *reinterpret_cast<floa
 __device__ __forceinline__ float4 ld4_stream(const float* p) { return __ldcs(reinterpret_cast<const float4*>(p)); }
 __device__ __forceinline__ void st4_stream(float* p, float4 v) { __stcs(reinterpret_cast<float4*>(p), v); }
 
+// ---------------------------------------------------------------------------
+// mbarrier helpers for bulk copies (TMA). Every wait is bounded: after
+// kWaitSpins polls it sets kErrWaitTimeout in the device error word and gives
+// up, so a lost completion surfaces as an error at the next sync instead of a
+// hung kernel.
+// ---------------------------------------------------------------------------
+constexpr long long kWaitSpins = 1ll << 24;
+
+__device__ __forceinline__ unsigned smem_addr(const void* p) {
+    return static_cast<unsigned>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(unsigned long long* bar, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+// Order this CTA's earlier generic-proxy accesses of shared memory before
+// later async-proxy (bulk copy) writes to it.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(unsigned long long* bar, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned parity) {
+    unsigned ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Wait for phase `parity` with an iteration limit; false (and the device
+// error bit) when it gave up.
+__device__ __forceinline__ bool mbar_wait_bounded(unsigned long long* bar, unsigned parity, unsigned* err) {
+    for (long long i = 0; i < kWaitSpins; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    atomicOr(err, kErrWaitTimeout);
+    return false;
+}
+
 // Max/argmax candidate under the reference's scan semantics: a larger value
 // wins; equal values (==, so -0 == +0) keep the smaller index; NaN is never
 // a candidate (the caller applies the "NaN at index 0 wins" rule).
