@@ -634,8 +634,7 @@ constexpr std::size_t kFMaxSmem = 112 * 1024;
 
 struct FusedDesc {
     int rank_g, rank_a;          // tensor-map ranks
-    int ucoord_g, ucoord_a;      // coordinate index of U1 in each map (then U0, then K)
-    int has_u0, nk;
+    int nk;
     unsigned U0, U1;
     FastDiv u1fd;
     long long ua0, ua1;          // da (= a layout) strides of the U dims
@@ -650,38 +649,30 @@ struct FusedDesc {
     unsigned VS, US, NV;         // slot split: v-slots, u-slots, v's per slot
     unsigned vs_log2, tp_log2;   // log2 of VS and of the threads per da output
     unsigned stage_bytes;        // one step: US tiles of g ([V][32]) and of a ([32])
+    unsigned scratch_floats;     // one da-partial buffer: [US * 32 outputs][VS + 1]
     unsigned long long db_count; // elements of db (the partial stride)
     double* da_d;                // unrounded outputs (shard partials) when set
     double* db_d;
     unsigned* err;               // device error word (bounded waits)
 };
 
-// Tiled TMA load (no multicast) of one box into this CTA's shared memory.
-__device__ __forceinline__ void tma_load(void* dst, const CUtensorMap* map, int rank, const int* c,
-                                         unsigned long long* bar) {
+// Tiled TMA load (no multicast) of one box into this CTA's shared memory;
+// coordinates innermost first, those beyond `rank` ignored.
+__device__ __forceinline__ void tma_load(void* dst, const CUtensorMap* map, int rank, int c0, int c1, int c2, int c3,
+                                         int c4, unsigned long long* bar) {
     const unsigned d = smem_addr(dst), b = smem_addr(bar);
     const unsigned long long m = reinterpret_cast<unsigned long long>(map);
-    switch (rank) {
-        case 2:
-            asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-                         " [%0], [%1, {%2, %3}], [%4];" ::"r"(d), "l"(m), "r"(c[0]), "r"(c[1]), "r"(b) : "memory");
-            break;
-        case 3:
-            asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-                         " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(d), "l"(m), "r"(c[0]), "r"(c[1]), "r"(c[2]),
-                         "r"(b) : "memory");
-            break;
-        case 4:
-            asm volatile("cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-                         " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(d), "l"(m), "r"(c[0]), "r"(c[1]), "r"(c[2]),
-                         "r"(c[3]), "r"(b) : "memory");
-            break;
-        default:
-            asm volatile("cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-                         " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(d), "l"(m), "r"(c[0]), "r"(c[1]), "r"(c[2]),
-                         "r"(c[3]), "r"(c[4]), "r"(b) : "memory");
-            break;
-    }
+    if (rank == 3)
+        asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                     " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(d), "l"(m), "r"(c0), "r"(c1), "r"(c2), "r"(b) : "memory");
+    else if (rank == 4)
+        asm volatile("cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                     " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(d), "l"(m), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+                     "r"(b) : "memory");
+    else
+        asm volatile("cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                     " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(d), "l"(m), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+                     "r"(c4), "r"(b) : "memory");
 }
 
 __device__ __forceinline__ long long decode_vb(const FusedDesc& d, unsigned v) {
@@ -709,7 +700,7 @@ bcast_backward_fused(const __grid_constant__ CUtensorMap gmap, const __grid_cons
     const unsigned g_tile = d.V * kFChunk;  // floats of one g tile
     double* dacc = reinterpret_cast<double*>(fsm + kFStages * d.stage_bytes);
     const unsigned acc_count = d.US * d.V * kFChunk;
-    float* scratch = reinterpret_cast<float*>(dacc + acc_count);
+    float* scratch = reinterpret_cast<float*>(dacc + acc_count);  // [2][scratch_floats]
     __shared__ unsigned long long full[kFStages];
     __shared__ long long s_uao[2][kFSlots];  // da offset of each u-slot's u, by step parity
 
@@ -752,6 +743,14 @@ bcast_backward_fused(const __grid_constant__ CUtensorMap gmap, const __grid_cons
     }
     __syncthreads();
 
+    // Tensor-map coordinates beyond (L, U1, U0): g has the V dims (always 0)
+    // then the K dims, innermost first; a has the K dims, innermost first.
+    int gk[2] = {0, 0}, ak[2] = {0, 0};
+    if (d.nk >= 1) {
+        ak[0] = kc[d.nk - 1];
+        if (d.nv == 1) gk[1] = kc[d.nk - 1];
+    }
+    if (d.nk == 2) ak[1] = kc[0];
     // producer (thread 0): step t -> stage t % kFStages, u = u0 + t*US + j
     unsigned p_c1 = 0, p_c0 = 0;  // U coordinates of the next u to issue
     unsigned issued = 0;          // steps issued
@@ -763,17 +762,12 @@ bcast_backward_fused(const __grid_constant__ CUtensorMap gmap, const __grid_cons
         mbar_expect_tx(&full[t % kFStages],
                        n * (g_tile + (NEED_A ? kFChunk : 0u)) * static_cast<unsigned>(sizeof(float)));
         for (unsigned j = 0; j < n; ++j) {
-            int cg_[5] = {static_cast<int>(l0), 0, 0, 0, 0};
-            int ca_[5] = {static_cast<int>(l0), 0, 0, 0, 0};
-            cg_[d.ucoord_g] = static_cast<int>(p_c1);
-            ca_[d.ucoord_a] = static_cast<int>(p_c1);
-            int ng = d.ucoord_g + 1, na = d.ucoord_a + 1;
-            if (d.has_u0) { cg_[ng++] = static_cast<int>(p_c0); ca_[na++] = static_cast<int>(p_c0); }
-            for (int i = d.nk - 1; i >= 0; --i) { cg_[ng++] = kc[i]; ca_[na++] = kc[i]; }  // innermost first
-            tma_load(reinterpret_cast<float*>(st) + j * g_tile, &gmap, d.rank_g, cg_, &full[t % kFStages]);
+            const int x = static_cast<int>(l0), c1 = static_cast<int>(p_c1), c0 = static_cast<int>(p_c0);
+            tma_load(reinterpret_cast<float*>(st) + j * g_tile, &gmap, d.rank_g, x, c1, c0, gk[0], gk[1],
+                     &full[t % kFStages]);
             if (NEED_A)
-                tma_load(reinterpret_cast<float*>(st) + d.US * g_tile + j * kFChunk, &amap, d.rank_a, ca_,
-                         &full[t % kFStages]);
+                tma_load(reinterpret_cast<float*>(st) + d.US * g_tile + j * kFChunk, &amap, d.rank_a, x, c1, c0,
+                         ak[0], ak[1], &full[t % kFStages]);
             if (++p_c1 == d.U1) { p_c1 = 0; ++p_c0; }
         }
         ++issued;
@@ -789,7 +783,7 @@ bcast_backward_fused(const __grid_constant__ CUtensorMap gmap, const __grid_cons
     float4 facc[kFMaxNV];
 #pragma unroll
     for (unsigned i = 0; i < kFMaxNV; ++i) facc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    const unsigned tp = 1u << d.tp_log2, per = d.VS >> d.tp_log2;
+    const unsigned tp = 1u << d.tp_log2;  // slot lanes per da output in the combine
     // Only thread 0 polls a stage's mbarrier (512 threads polling one word
     // would crowd the shared-memory pipe); the CTA barrier that follows
     // publishes the stage, and the success flag, to every thread.
@@ -818,9 +812,12 @@ bcast_backward_fused(const __grid_constant__ CUtensorMap gmap, const __grid_cons
                 facc[i] = add4(facc[i], gb);
             }
         }
-        // da: the VS slots of each u, combined in a fixed tree
-        float* sc = scratch + (t & 1u) * kFSlots * kFChunk;
-        reinterpret_cast<float4*>(sc)[slot * kFLanes + lane] = dap;
+        // da: the VS slots of each u, combined in a fixed tree. Partials go
+        // to [slot][32] rows with the float4 column XOR-swizzled by slot % 8,
+        // so both this store and the combine's reads (4 outputs x 8 slots per
+        // warp instruction) are free of bank conflicts.
+        float* sc = scratch + (t & 1u) * d.scratch_floats;
+        reinterpret_cast<float4*>(sc)[slot * kFLanes + (lane ^ (slot & 7u))] = dap;
         if (vs == 0 && lane == 0) s_uao[t & 1u][us] = uao;
         bool next_ok = ok;
         if (threadIdx.x == 0 && ok && t + 1 < nsteps) {
@@ -833,15 +830,21 @@ bcast_backward_fused(const __grid_constant__ CUtensorMap gmap, const __grid_cons
             fence_proxy_async_smem();
             issue(t + kFStages);
         }
-        for (unsigned w = threadIdx.x; w < (d.US * kFChunk) << d.tp_log2; w += kFThreads) {
-            const unsigned o = w >> d.tp_log2, sub = w & (tp - 1);
+        // A warp pass covers go = 32 / gs outputs x gs slot lanes (gs =
+        // min(VS, 8)); lane (j, k) adds slots j, j + gs, ... of its output in
+        // double, then the gs lanes meet in a double xor tree.
+        for (unsigned o0 = (threadIdx.x >> 5) * (32u >> d.tp_log2); o0 < d.US * kFChunk;
+             o0 += (kFThreads / 32) * (32u >> d.tp_log2)) {
+            const unsigned go = 32u >> d.tp_log2;
+            const unsigned o = o0 + ((threadIdx.x & 31) & (go - 1)), j = (threadIdx.x & 31) >> (5 - d.tp_log2);
             const unsigned ou = o / kFChunk, ol = o % kFChunk;
-            const float* src = sc + ((ou << d.vs_log2) + sub * per) * kFChunk + ol;
-            float f = src[0];
-            for (unsigned x = 1; x < per; ++x) f += src[x * kFChunk];
-            double s = static_cast<double>(f);
-            for (unsigned m = 1; m < tp; m <<= 1) s += __shfl_xor_sync(0xffffffffu, s, m);
-            if (sub == 0 && u0 + ou + t * d.US < u1 && l0 + ol < d.L) {
+            double s = 0.0;
+            for (unsigned v = j; v < d.VS; v += tp) {
+                const unsigned sl = ou * d.VS + v;
+                s += static_cast<double>(sc[sl * kFChunk + ((((ol >> 2) ^ (sl & 7u)) << 2) | (ol & 3u))]);
+            }
+            for (unsigned m = go; m < 32; m <<= 1) s += __shfl_xor_sync(0xffffffffu, s, m);
+            if (j == 0 && u0 + ou + t * d.US < u1 && l0 + ol < d.L) {
                 const long long off = ka + s_uao[t & 1u][ou] + static_cast<long long>(l0 + ol);
                 if (d.da_d) d.da_d[off] = s;
                 else da[off] = static_cast<float>(s);
@@ -999,33 +1002,30 @@ static bool try_fused_bcast_backward(int op, const float* a, const Src& sa, cons
     for (int i = 0; i < nk; ++i) { d.kdims[i] = kd[i].size; d.ka[i] = kd[i].st[1]; d.kb[i] = kd[i].st[2]; }
     // U as (U0 outer, U1 inner); one U dim is (1, U)
     const Dim uinner = ud[nu - 1];
-    d.has_u0 = nu == 2;
+    const Dim uouter = nu == 2 ? ud[0] : Dim{2, 1, {uinner.st[0] * static_cast<long long>(uinner.size),
+                                                    uinner.st[1] * static_cast<long long>(uinner.size), 0}};
     d.U1 = static_cast<unsigned>(uinner.size);
-    d.U0 = nu == 2 ? static_cast<unsigned>(ud[0].size) : 1u;
+    d.U0 = static_cast<unsigned>(uouter.size);
     d.u1fd = FastDiv(d.U1);
     d.ua1 = uinner.st[1];
-    d.ua0 = nu == 2 ? ud[0].st[1] : 0;
-    // tensor maps, dims innermost first. g: (L, V dims, U1, [U0], K dims);
-    // a: (L, U1, [U0], K dims). Boxes: 32 floats x all of V; 32 floats.
+    d.ua0 = uouter.st[1];
+    // tensor maps, dims innermost first. g: (L, U1, U0, V dims, K dims);
+    // a: (L, U1, U0, K dims). Boxes: 32 floats x 1 x 1 x all of V; 32 floats.
+    if (3 + nv + nk > 5) return false;
     unsigned long long gdims[5], adims[5];
     long long gstr[5], astr[5];
     unsigned gbox[5], abox[5];
     int rg = 0, ra = 0;
     gdims[rg] = d.L; gstr[rg] = 1; gbox[rg++] = kFChunk;
+    adims[ra] = d.L; astr[ra] = 1; abox[ra++] = kFChunk;
+    gdims[rg] = uinner.size; gstr[rg] = uinner.st[0]; gbox[rg++] = 1;
+    adims[ra] = uinner.size; astr[ra] = uinner.st[1]; abox[ra++] = 1;
+    gdims[rg] = uouter.size; gstr[rg] = uouter.st[0]; gbox[rg++] = 1;
+    adims[ra] = uouter.size; astr[ra] = uouter.st[1]; abox[ra++] = 1;
     for (int i = nv - 1; i >= 0; --i) {
         gdims[rg] = vd[i].size; gstr[rg] = vd[i].st[0]; gbox[rg++] = static_cast<unsigned>(vd[i].size);
     }
-    adims[ra] = d.L; astr[ra] = 1; abox[ra++] = kFChunk;
-    d.ucoord_g = rg;
-    d.ucoord_a = ra;
-    gdims[rg] = uinner.size; gstr[rg] = uinner.st[0]; gbox[rg++] = 1;
-    adims[ra] = uinner.size; astr[ra] = uinner.st[1]; abox[ra++] = 1;
-    if (nu == 2) {
-        gdims[rg] = ud[0].size; gstr[rg] = ud[0].st[0]; gbox[rg++] = 1;
-        adims[ra] = ud[0].size; astr[ra] = ud[0].st[1]; abox[ra++] = 1;
-    }
     for (int i = nk - 1; i >= 0; --i) {
-        if (rg == 5 || ra == 5) return false;
         gdims[rg] = kd[i].size; gstr[rg] = kd[i].st[0]; gbox[rg++] = 1;
         adims[ra] = kd[i].size; astr[ra] = kd[i].st[1]; abox[ra++] = 1;
     }
@@ -1039,12 +1039,13 @@ static bool try_fused_bcast_backward(int op, const float* a, const Src& sa, cons
     d.VS = vs;
     d.US = kFSlots / vs;
     d.NV = static_cast<unsigned>((V + vs - 1) / vs);
-    const unsigned tp = std::max(1u, std::min(vs, kFThreads / (d.US * kFChunk)));
+    const unsigned tp = std::min(vs, 8u);
     d.vs_log2 = 0;
     while ((1u << d.vs_log2) < vs) ++d.vs_log2;
     d.tp_log2 = 0;
     while ((1u << d.tp_log2) < tp) ++d.tp_log2;
     d.stage_bytes = d.US * (d.V + 1) * kFChunk * static_cast<unsigned>(sizeof(float));
+    d.scratch_floats = kFSlots * kFChunk;
     const unsigned long long chunks = (d.L + kFChunk - 1) / kFChunk;
     unsigned long long S = (kFTargetCtas + chunks * K - 1) / (chunks * K);
     S = std::min<unsigned long long>(S, (U + kFMinUSeg - 1) / kFMinUSeg);
@@ -1059,7 +1060,7 @@ static bool try_fused_bcast_backward(int op, const float* a, const Src& sa, cons
     d.err = device_error_word();
     const std::size_t smem = kFStages * static_cast<std::size_t>(d.stage_bytes) +
                              static_cast<std::size_t>(d.US) * d.V * kFChunk * sizeof(double) +
-                             2 * kFSlots * kFChunk * sizeof(float);
+                             2 * static_cast<std::size_t>(d.scratch_floats) * sizeof(float);
     if (smem > kFMaxSmem) return false;
     Scratch partial(d.S > 1 ? static_cast<std::size_t>(d.S) * b_numel * sizeof(double) : 8);
     const dim3 grid(static_cast<unsigned>(chunks), d.S, static_cast<unsigned>(K));
