@@ -268,6 +268,42 @@ vc_status vc_cuda_cross_entropy_backward(const float* logits, const int64_t* tar
                                          const float* upstream, size_t batch, size_t classes,
                                          size_t batch_total, float* dlogits);
 
+/* ---- CUDA graphs ------------------------------------------------------------
+ * No counterpart in the reference (Metal encodes one command buffer per op,
+ * src/metal/metal_backend.mm). Capture the library stream's work between
+ * begin and end into a replayable graph: launch-bound chains (config 1) then
+ * cost one launch. Every pool block allocated during the capture belongs to
+ * the graph: it may be reused within the capture, and once freed after it
+ * stays reserved (replays still use it) until vc_cuda_graph_destroy returns
+ * it to the pool. Tensors created during the capture hold the buffers each
+ * replay rewrites. Anything that synchronises the stream (download,
+ * vc_cuda_synchronize, matmul) cannot be captured: vc_cuda_graph_end then
+ * fails and the capture is discarded. One capture at a time per process. */
+vc_status vc_cuda_graph_begin(void);
+vc_status vc_cuda_graph_end(void** graph);
+vc_status vc_cuda_graph_launch(void* graph);          /* enqueue one replay */
+vc_status vc_cuda_graph_nodes(void* graph, size_t* nodes);
+vc_status vc_cuda_graph_destroy(void* graph);
+
+/* ---- fused forward chains ---------------------------------------------------
+ * relu(x + b).sum() for x [rows, cols] and a row-broadcast bias b [cols], as
+ * ONE launch each way. Replaces the reference's op-by-op chain
+ * binary_forward (src/ops.cpp:27-41) -> relu (:395-403) -> sum (:288-302)
+ * and its backward broadcast_to -> relu backward -> sum_to_shape
+ * (src/autograd.cpp:50-91) for this pattern. */
+
+/* loss[0] = float(sum of relu(x + b)); loss_partial[0] (optional) = the
+ * unrounded double sum (a shard's partial). Either output may be null, not
+ * both. */
+vc_status vc_cuda_bias_relu_sum(const float* x, const float* b, size_t rows, size_t cols, float* loss,
+                                double* loss_partial);
+/* Given the upstream gradient u (device scalar) of the sum:
+ * dx = (u + 0) * (x + b > 0 ? 1 : 0) (bit-exact with the reference),
+ * db[j] = float(sum over rows of dx[:, j]), or db_partial[j] unrounded when
+ * db is null. */
+vc_status vc_cuda_bias_relu_sum_backward(const float* x, const float* b, const float* upstream, size_t rows,
+                                         size_t cols, float* dx, float* db, double* db_partial);
+
 /* ---- multi-GPU: leading-axis shards, partials combined in rank order -----
  * No counterpart in the reference (it is single-device). One process per
  * GPU; each rank reduces its shard into an unrounded partial, the partials

@@ -368,6 +368,40 @@ def test_config1_pipeline_matches_reference_golden(golden):
     assert_sum_close(b.grad.numpy(), golden["cfg1_full/db"], x_np.shape[0], 1.0)
 
 
+def test_fused_bias_relu_sum_matches_reference_golden(golden):
+    """The one-launch fused chain gives the reference's configuration-1
+    results: dx and db bit for bit, the loss within the sum tolerance."""
+    x_np, b_np = C.cfg1()
+    x, b = T(x_np, True), T(b_np, True)
+    loss = vc.bias_relu_sum(x, b)
+    loss.backward()
+    assert sha256(x.grad.numpy()) == str(golden["cfg1_full/dx/sha256"])
+    assert_sum_close(loss.item(), golden["cfg1_full/loss"], x_np.size, 1.0)
+    assert_bitexact(b.grad.numpy(), golden["cfg1_full/db"], "db")
+
+
+@pytest.mark.parametrize("shape", [(1, 1), (3, 5), (65, 130), (200, 4100), (1000, 8)])
+def test_fused_bias_relu_sum_matches_composed_ops(shape):
+    """Odd column counts (scalar path), rows across several 64-row segments,
+    columns across several 1024-column blocks, and a non-unit upstream."""
+    rng = np.random.default_rng(shape[0] * 7 + shape[1])
+    x_np = rng.uniform(-1, 1, shape).astype(np.float32)
+    b_np = rng.normal(size=shape[1]).astype(np.float32)
+    x1, b1 = T(x_np, True), T(b_np, True)
+    fused = vc.bias_relu_sum(x1, b1) * 0.37
+    fused.backward()
+    x2, b2 = T(x_np, True), T(b_np, True)
+    composed = (x2 + b2).relu().sum() * 0.37
+    composed.backward()
+    assert_sum_close(fused.item(), composed.item(), x_np.size, 1.0)
+    assert_bitexact(x1.grad.numpy(), x2.grad.numpy(), "dx")
+    # db is g times an exact row count: the same bits as the double sum
+    assert_bitexact(b1.grad.numpy(), b2.grad.numpy(), "db")
+    for _ in range(2):  # the ticket counters reset themselves: repeat calls agree
+        again = vc.bias_relu_sum(x1, b1).item()
+        assert again == vc.bias_relu_sum(x1, b1).item()
+
+
 def test_config5_pipeline_matches_reference_golden(golden):
     a_np, b_np = C.cfg5(C.SMALL["cfg5"]["a"], C.SMALL["cfg5"]["b"])
     a, b = T(a_np, True), T(b_np, True)

@@ -11,8 +11,8 @@ from . import _abi
 from ._abi import available as cuda_available  # noqa: F401
 from ._abi import device_name as cuda_device_name  # noqa: F401
 from .nn import Linear, mse_loss, sgd_step, zero_grad  # noqa: F401
-from .tensor import (NoGradGuard, Tensor, argmax_int64, cross_entropy, grad_enabled, log_softmax,  # noqa: F401
-                     no_grad, softmax)
+from .tensor import (NoGradGuard, Tensor, argmax_int64, bias_relu_sum, cross_entropy, grad_enabled,  # noqa: F401
+                     log_softmax, no_grad, softmax)
 
 
 def synchronize() -> None:

@@ -99,6 +99,13 @@ _SIGS = {
     "vc_cuda_softmax_backward": (c_int, [_f, _f, _f, _f, _f, c_size_t, c_size_t, c_size_t]),
     "vc_cuda_cross_entropy": (c_int, [_f, c_void_p, c_size_t, c_size_t, c_size_t, _f, _f, _f, c_void_p]),
     "vc_cuda_cross_entropy_backward": (c_int, [_f, c_void_p, _f, _f, _f, c_size_t, c_size_t, c_size_t, _f]),
+    "vc_cuda_bias_relu_sum": (c_int, [_f, _f, c_size_t, c_size_t, _f, c_void_p]),
+    "vc_cuda_graph_begin": (c_int, []),
+    "vc_cuda_graph_end": (c_int, [POINTER(c_void_p)]),
+    "vc_cuda_graph_launch": (c_int, [c_void_p]),
+    "vc_cuda_graph_nodes": (c_int, [c_void_p, POINTER(c_size_t)]),
+    "vc_cuda_graph_destroy": (c_int, [c_void_p]),
+    "vc_cuda_bias_relu_sum_backward": (c_int, [_f, _f, _f, c_size_t, c_size_t, _f, _f, c_void_p]),
     "vc_cuda_matmul": (c_int, [_f, _f, _f, c_size_t, c_size_t, c_size_t, _szp, _szp, c_size_t, c_int, c_int]),
     "vc_cuda_transpose_last2": (c_int, [_f, _f, c_size_t, c_size_t, c_size_t]),
     "vc_cuda_reduce_sum_noalloc": (c_int, [_f, c_size_t, _f]),

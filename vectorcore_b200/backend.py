@@ -64,6 +64,38 @@ def _p(x):
     return None if x is None else ctypes.c_void_p(x.ptr)
 
 
+class CudaGraph:
+    """A replayable capture of the library stream's work (vc_cuda_graph_*).
+    The pool blocks allocated while capturing stay reserved for the graph
+    until close(); storages returned by the captured calls are rewritten by
+    every replay."""
+
+    def __init__(self, handle: int):
+        self._h = ctypes.c_void_p(handle)
+
+    def launch(self) -> None:
+        if not self._h.value:
+            raise RuntimeError("CudaGraph: launch after close()")
+        _abi.call("vc_cuda_graph_launch", self._h)
+
+    @property
+    def nodes(self) -> int:
+        n = ctypes.c_size_t(0)
+        _abi.call("vc_cuda_graph_nodes", self._h, ctypes.byref(n))
+        return int(n.value)
+
+    def close(self) -> None:
+        if self._h.value:
+            _abi.call("vc_cuda_graph_destroy", self._h)
+            self._h = ctypes.c_void_p(0)
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class CudaBackend:
     _instance = None
     _lock = threading.Lock()
@@ -87,6 +119,25 @@ class CudaBackend:
 
     def synchronize(self) -> None:
         _abi.synchronize()
+
+    def capture(self, fn):
+        """Run fn() under stream capture; returns (CudaGraph, fn's result).
+        The captured work is NOT executed by the capture itself: launch the
+        graph to run it."""
+        _abi.call("vc_cuda_graph_begin")
+        try:
+            result = fn()
+        except BaseException:
+            h = ctypes.c_void_p(0)
+            try:
+                _abi.call("vc_cuda_graph_end", ctypes.byref(h))
+            finally:
+                if h.value:
+                    _abi.call("vc_cuda_graph_destroy", h)
+            raise
+        h = ctypes.c_void_p(0)
+        _abi.call("vc_cuda_graph_end", ctypes.byref(h))
+        return CudaGraph(h.value), result
 
     # ---- memory ---------------------------------------------------------------
     def allocate(self, elements: int, dtype=np.float32) -> CudaStorage:
@@ -253,3 +304,19 @@ class CudaBackend:
         _abi.call("vc_cuda_cross_entropy_backward", _p(logits), _p(targets), _p(m), _p(s), _p(upstream),
                   ctypes.c_size_t(batch), ctypes.c_size_t(classes), ctypes.c_size_t(batch_total), _p(dx))
         return dx
+
+    # ---- fused chain relu(x + b).sum() (one launch each way) ----------------
+    def bias_relu_sum(self, x, b, rows, cols):
+        """loss storage (1 element) = relu(x + b).sum() for x [rows, cols], b [cols]."""
+        loss = CudaStorage(1)
+        _abi.call("vc_cuda_bias_relu_sum", _p(x), _p(b), ctypes.c_size_t(rows), ctypes.c_size_t(cols), _p(loss),
+                  None)
+        return loss
+
+    def bias_relu_sum_backward(self, x, b, upstream, rows, cols):
+        """(dx, db) of relu(x + b).sum() given the upstream scalar gradient."""
+        dx = CudaStorage(rows * cols)
+        db = CudaStorage(cols)
+        _abi.call("vc_cuda_bias_relu_sum_backward", _p(x), _p(b), _p(upstream), ctypes.c_size_t(rows),
+                  ctypes.c_size_t(cols), _p(dx), _p(db), None)
+        return dx, db

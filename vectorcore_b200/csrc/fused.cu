@@ -1,0 +1,246 @@
+// fused.cu -- fused forward chains for sm_100a: relu(x + b).sum() for a
+// row-broadcast bias b, forward and backward, each ONE launch.
+//
+// The reference runs the chain as separate ops with a full-size temporary per
+// step (src/ops.cpp:27-52 add, :395-403 relu, :288-302 sum) and its backward
+// as broadcast_to + relu backward + sum_to_shape (src/autograd.cpp:50-91):
+// five to seven passes. Here the forward reads x and b once; the backward
+// recomputes h = x + b (the same float add, so the same bits) instead of
+// reading a saved h, writes dx once and reduces db in the same pass.
+//
+// Arithmetic, as the reference:
+//   h = x + b;  y = h > 0 ? h : 0;  loss = float(sum of y)
+//   g = u + 0 (broadcast_to of the upstream scalar);  dx = g * (h > 0 ? 1 : 0)
+//   db[j] = float(sum over rows of dx[i, j])
+// dx and db are bit-exact (db from exact integer counts, see db_from_count).
+// The loss sum is double (groups of four terms in float, then double) over
+// shape-derived splits finished by the last CTA to arrive (a ticket counter)
+// in a fixed order, so it does not depend on timing.
+#include "vc_internal.cuh"
+
+#include <algorithm>
+
+namespace vc {
+
+namespace {
+
+constexpr unsigned kThreads = 256;
+constexpr unsigned kTicketForward = 0;        // ticket counter slots
+constexpr unsigned kTicketBackward = 1;
+constexpr unsigned kFwdPerThread = 4;         // forward: float4 groups per thread (in flight together)
+constexpr unsigned kBwdSegRows = 16;          // backward: rows per CTA
+constexpr unsigned kBwdColBlock = kThreads * 4;  // backward: columns per CTA (float4 lanes)
+
+__device__ __forceinline__ float relu_of(float h) { return h > 0.0f ? h : 0.0f; }
+
+// Last CTA to arrive (ticket == expected - 1) sees every CTA's partial.
+__device__ __forceinline__ bool arrive_last(unsigned* ticket, unsigned expected, bool* s_last) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        *s_last = atomicAdd(ticket, 1u) == expected - 1;
+    }
+    __syncthreads();
+    if (*s_last) __threadfence();
+    return *s_last;
+}
+
+// Forward over x viewed flat: CTA k owns the 1024 float4 groups (or
+// elements) [k * 1024, ...); thread t adds groups t, t + 256, t + 512,
+// t + 768 of them (four loads in flight), each group's bias from its column.
+// The last CTA adds the per-CTA partials in order.
+template <bool VEC>
+__global__ void __launch_bounds__(kThreads)
+bias_relu_sum_fwd(const float* __restrict__ x, const float* __restrict__ b, unsigned long long units,
+                  unsigned long long cols_units, FastDiv cols_fd, bool cols_small, double* __restrict__ partial,
+                  unsigned* __restrict__ ticket, float* __restrict__ loss, double* __restrict__ loss_d) {
+    __shared__ double s_red[32];
+    __shared__ bool s_last;
+    const unsigned long long base = static_cast<unsigned long long>(blockIdx.x) * kThreads * kFwdPerThread;
+    auto col_of = [&](unsigned long long e) -> unsigned long long {
+        if (cols_small) {  // e < 2^32: FastDiv
+            unsigned q, r;
+            cols_fd.divmod(static_cast<unsigned>(e), q, r);
+            return r;
+        }
+        return e % cols_units;
+    };
+    double acc = 0.0;
+    if constexpr (VEC) {
+        float4 xv[kFwdPerThread], bv[kFwdPerThread];
+        bool ok[kFwdPerThread];
+#pragma unroll
+        for (unsigned k = 0; k < kFwdPerThread; ++k) {
+            const unsigned long long e = base + k * kThreads + threadIdx.x;
+            ok[k] = e < units;
+            if (ok[k]) {
+                xv[k] = ldg4(x + 4 * e);
+                bv[k] = ldg4(b + 4 * col_of(e));
+            }
+        }
+#pragma unroll
+        for (unsigned k = 0; k < kFwdPerThread; ++k) {
+            if (!ok[k]) continue;
+            const float y0 = relu_of(xv[k].x + bv[k].x), y1 = relu_of(xv[k].y + bv[k].y);
+            const float y2 = relu_of(xv[k].z + bv[k].z), y3 = relu_of(xv[k].w + bv[k].w);
+            acc += static_cast<double>((y0 + y1) + (y2 + y3));
+        }
+    } else {
+#pragma unroll
+        for (unsigned k = 0; k < kFwdPerThread; ++k) {
+            const unsigned long long e = base + k * kThreads + threadIdx.x;
+            if (e < units) acc += static_cast<double>(relu_of(__ldg(x + e) + __ldg(b + col_of(e))));
+        }
+    }
+    acc = block_sum(acc, s_red);
+    if (threadIdx.x == 0) partial[blockIdx.x] = acc;
+    if (!arrive_last(ticket, gridDim.x, &s_last)) return;
+    double t = 0.0;
+    for (unsigned s = threadIdx.x; s < gridDim.x; s += kThreads) t += __ldcg(partial + s);
+    t = block_sum(t, s_red);
+    if (threadIdx.x == 0) {
+        if (loss) *loss = static_cast<float>(t);
+        if (loss_d) *loss_d = t;
+        *ticket = 0;  // ready for the next launch (stream order)
+    }
+}
+
+// db[j] from the count of rows with x + b > 0. Every dx[i, j] is g * 1 = g or
+// g * 0 = +-0, so the reference's double sum over rows is g * count exactly
+// (no rounding while count < 2^29: 24 + 29 bits), +0 for a zero count (the
+// sum starts at +0), NaN for a NaN g, and for an infinite g +-inf only when
+// every row contributes g (inf * 0 is NaN).
+__device__ __forceinline__ double db_from_count(float g, unsigned long long count, unsigned long long rows) {
+    if (g != g) return static_cast<double>(g);
+    if (isinf(g)) return count == rows ? static_cast<double>(g) : static_cast<double>(__int_as_float(0x7fc00000));
+    if (count == 0) return 0.0;
+    return static_cast<double>(g) * static_cast<double>(count);
+}
+
+// Backward. grid = (column blocks, row segments). Thread t of column block cb
+// owns float4 column cb*256 + t (or columns cb*1024 + t + 256k) over the
+// CTA's rows: writes dx and counts its rows with h > 0; the counts go to
+// `counts` with integer atomics (exact in any order), and the last CTA
+// converts them to db and clears them.
+template <bool VEC>
+__global__ void __launch_bounds__(kThreads)
+bias_relu_sum_bwd(const float* __restrict__ x, const float* __restrict__ b, const float* __restrict__ upstream,
+                  unsigned long long rows, unsigned long long cols, float* __restrict__ dx, float* __restrict__ db,
+                  double* __restrict__ db_d, unsigned* __restrict__ counts, unsigned* __restrict__ ticket) {
+    __shared__ bool s_last;
+    const float g = __ldg(upstream) + 0.0f;  // broadcast_to(u): u + 0
+    const unsigned long long r0 = static_cast<unsigned long long>(blockIdx.y) * kBwdSegRows;
+    const unsigned long long r1 = min(rows, r0 + kBwdSegRows);
+    const unsigned long long c0 = static_cast<unsigned long long>(blockIdx.x) * kBwdColBlock;
+    if constexpr (VEC) {
+        const unsigned long long c = c0 + 4ull * threadIdx.x;
+        if (c < cols) {
+            const float4 bv = ldg4(b + c);
+            unsigned n0 = 0, n1 = 0, n2 = 0, n3 = 0;
+#pragma unroll 8
+            for (unsigned long long r = r0; r < r1; ++r) {
+                const float4 xv = ldg4(x + r * cols + c);
+                const bool p0 = (xv.x + bv.x) > 0.0f, p1 = (xv.y + bv.y) > 0.0f;
+                const bool p2 = (xv.z + bv.z) > 0.0f, p3 = (xv.w + bv.w) > 0.0f;
+                st4_stream(dx + r * cols + c, make_float4(g * (p0 ? 1.0f : 0.0f), g * (p1 ? 1.0f : 0.0f),
+                                                          g * (p2 ? 1.0f : 0.0f), g * (p3 ? 1.0f : 0.0f)));
+                n0 += p0;
+                n1 += p1;
+                n2 += p2;
+                n3 += p3;
+            }
+            if (n0) atomicAdd(counts + c, n0);
+            if (n1) atomicAdd(counts + c + 1, n1);
+            if (n2) atomicAdd(counts + c + 2, n2);
+            if (n3) atomicAdd(counts + c + 3, n3);
+        }
+    } else {
+        for (unsigned long long c = c0 + threadIdx.x; c < min(cols, c0 + kBwdColBlock); c += kThreads) {
+            const float bv = __ldg(b + c);
+            unsigned n = 0;
+            for (unsigned long long r = r0; r < r1; ++r) {
+                const bool p = (__ldg(x + r * cols + c) + bv) > 0.0f;
+                dx[r * cols + c] = g * (p ? 1.0f : 0.0f);
+                n += p;
+            }
+            if (n) atomicAdd(counts + c, n);
+        }
+    }
+    if (!arrive_last(ticket, gridDim.x * gridDim.y, &s_last)) return;
+    for (unsigned long long c = threadIdx.x; c < cols; c += kThreads) {
+        const unsigned count = __ldcg(counts + c);
+        counts[c] = 0;
+        const double v = db_from_count(g, count, rows);
+        if (db_d) db_d[c] = v;
+        else db[c] = static_cast<float>(v);
+    }
+    if (threadIdx.x == 0) *ticket = 0;
+}
+
+}  // namespace
+
+}  // namespace vc
+
+using namespace vc;
+
+extern "C" {
+
+vc_status vc_cuda_bias_relu_sum(const float* x, const float* b, size_t rows, size_t cols, float* loss,
+                                double* loss_partial) {
+    VC_API_BEGIN
+    ensure_init();
+    const size_t dims[2] = {rows, cols};
+    checked_numel(dims, 2);
+    if (!loss && !loss_partial) fail(VC_ERR_INVALID, "bias_relu_sum: null output");
+    if (!rows || !cols) {
+        if (loss) VC_CUDA(cudaMemsetAsync(loss, 0, sizeof(float), stream()));
+        if (loss_partial) VC_CUDA(cudaMemsetAsync(loss_partial, 0, sizeof(double), stream()));
+        return VC_OK;
+    }
+    if (!x || !b) fail(VC_ERR_INVALID, "bias_relu_sum: null input");
+    const bool vec = cols % 4 == 0 && aligned16(x) && aligned16(b);
+    const unsigned long long units = vec ? rows * cols / 4 : rows * cols;
+    const unsigned long long cols_units = vec ? cols / 4 : cols;
+    const unsigned long long ctas = (units + kThreads * kFwdPerThread - 1) / (kThreads * kFwdPerThread);
+    if (ctas > 0x7fffffffull) fail(VC_ERR_OVERFLOW, "bias_relu_sum: tensor too large");
+    const bool cols_small = units < (1ull << 32) && cols_units < (1ull << 32);
+    const FastDiv cols_fd(cols_small ? static_cast<unsigned>(cols_units) : 1u);
+    Scratch partial(ctas * sizeof(double));
+    unsigned* ticket = counters() + kTicketForward;
+    if (vec) bias_relu_sum_fwd<true><<<static_cast<unsigned>(ctas), kThreads, 0, stream()>>>(x, b, units, cols_units, cols_fd, cols_small, partial.as<double>(), ticket, loss, loss_partial);
+    else bias_relu_sum_fwd<false><<<static_cast<unsigned>(ctas), kThreads, 0, stream()>>>(x, b, units, cols_units, cols_fd, cols_small, partial.as<double>(), ticket, loss, loss_partial);
+    check_launch("bias_relu_sum");
+    VC_API_END
+}
+
+vc_status vc_cuda_bias_relu_sum_backward(const float* x, const float* b, const float* upstream, size_t rows,
+                                         size_t cols, float* dx, float* db, double* db_partial) {
+    VC_API_BEGIN
+    ensure_init();
+    const size_t dims[2] = {rows, cols};
+    checked_numel(dims, 2);
+    if (!cols) return VC_OK;
+    if (!db && !db_partial) fail(VC_ERR_INVALID, "bias_relu_sum_backward: null db");
+    if (!rows) {
+        if (db) VC_CUDA(cudaMemsetAsync(db, 0, cols * sizeof(float), stream()));
+        if (db_partial) VC_CUDA(cudaMemsetAsync(db_partial, 0, cols * sizeof(double), stream()));
+        return VC_OK;
+    }
+    if (!x || !b || !upstream || !dx) fail(VC_ERR_INVALID, "bias_relu_sum_backward: null pointer");
+    const unsigned long long col_blocks = (cols + kBwdColBlock - 1) / kBwdColBlock;
+    const unsigned long long segs = (rows + kBwdSegRows - 1) / kBwdSegRows;
+    if (col_blocks > 0x7fffffffull || segs > 65535 || col_blocks * segs > 0xffffffffull)
+        fail(VC_ERR_OVERFLOW, "bias_relu_sum_backward: tensor too large");
+    if (rows >= (1ull << 32)) fail(VC_ERR_OVERFLOW, "bias_relu_sum_backward: too many rows for 32-bit counts");
+    Scratch counts(cols * sizeof(unsigned));
+    VC_CUDA(cudaMemsetAsync(counts.as<unsigned>(), 0, cols * sizeof(unsigned), stream()));
+    const dim3 grid(static_cast<unsigned>(col_blocks), static_cast<unsigned>(segs));
+    unsigned* ticket = counters() + kTicketBackward;
+    const bool vec = cols % 4 == 0 && aligned16(x) && aligned16(b) && aligned16(dx);
+    if (vec) bias_relu_sum_bwd<true><<<grid, kThreads, 0, stream()>>>(x, b, upstream, rows, cols, dx, db, db_partial, counts.as<unsigned>(), ticket);
+    else bias_relu_sum_bwd<false><<<grid, kThreads, 0, stream()>>>(x, b, upstream, rows, cols, dx, db, db_partial, counts.as<unsigned>(), ticket);
+    check_launch("bias_relu_sum_backward");
+    VC_API_END
+}
+
+}  // extern "C"

@@ -32,8 +32,23 @@ namespace {
 
 thread_local std::string t_last_error;
 
+// A captured CUDA graph and the pool blocks it owns. Every block allocated
+// while the graph is being captured belongs to it: freed during the capture,
+// a block may serve a later allocation of the same capture (stream order);
+// freed after it, the block stays reserved -- the graph's replays still use
+// it -- until the graph is destroyed.
+struct GraphRecord {
+    cudaGraph_t graph{nullptr};
+    cudaGraphExec_t exec{nullptr};
+    std::map<std::size_t, std::vector<void*>> capture_free;  // reusable during capture
+    std::vector<std::pair<void*, std::size_t>> reserved;      // (block, bucket) freed after capture
+    std::size_t kernels{0};
+};
+
 struct Pool {
     std::mutex mutex;
+    GraphRecord* capturing{nullptr};
+    std::unordered_map<void*, GraphRecord*> owner;           // block -> graph that owns it
     std::map<std::size_t, std::vector<void*>> free_blocks;  // bucket bytes -> blocks
     std::unordered_map<void*, std::size_t> live;             // block -> bucket bytes
     std::size_t cached_bytes{0};
@@ -148,8 +163,21 @@ static void* pool_alloc(std::size_t bytes) {
     State& s = state();
     Pool& pool = s.pool;
     const std::size_t b = bucket_bytes(bytes ? bytes : 1);
+    GraphRecord* graph = nullptr;
     {
         std::lock_guard<std::mutex> lock(pool.mutex);
+        graph = pool.capturing;
+        if (graph) {
+            auto ct = graph->capture_free.find(b);
+            if (ct != graph->capture_free.end() && !ct->second.empty()) {
+                void* p = ct->second.back();
+                ct->second.pop_back();
+                pool.in_use_bytes += b;
+                pool.live[p] = b;
+                ++pool.hits;
+                return p;
+            }
+        }
         auto it = pool.free_blocks.find(b);
         if (it != pool.free_blocks.end() && !it->second.empty()) {
             void* p = it->second.back();
@@ -157,6 +185,7 @@ static void* pool_alloc(std::size_t bytes) {
             pool.cached_bytes -= b;
             pool.in_use_bytes += b;
             pool.live[p] = b;
+            if (graph) pool.owner[p] = graph;
             ++pool.hits;
             return p;
         }
@@ -165,7 +194,7 @@ static void* pool_alloc(std::size_t bytes) {
     if (std::getenv("VC_CUDA_FAKE_OOM")) fail(VC_ERR_OOM, "device allocation failed (VC_CUDA_FAKE_OOM)");
     void* p = nullptr;
     cudaError_t err = cudaMalloc(&p, b);
-    if (err == cudaErrorMemoryAllocation) {
+    if (err == cudaErrorMemoryAllocation && !graph) {
         cudaGetLastError();
         // Cached blocks may still be referenced by enqueued work: finish it,
         // hand the cache back to the driver and retry once.
@@ -184,6 +213,7 @@ static void* pool_alloc(std::size_t bytes) {
     std::lock_guard<std::mutex> lock(pool.mutex);
     pool.in_use_bytes += b;
     pool.live[p] = b;
+    if (graph) pool.owner[p] = graph;
     return p;
 }
 
@@ -197,6 +227,13 @@ static void pool_free(void* p) {
     const std::size_t b = it->second;
     pool.live.erase(it);
     pool.in_use_bytes -= b;
+    auto own = pool.owner.find(p);
+    if (own != pool.owner.end()) {
+        GraphRecord* g = own->second;
+        if (g == pool.capturing) g->capture_free[b].push_back(p);
+        else g->reserved.emplace_back(p, b);
+        return;
+    }
     if (pool.cached_bytes + b > pool.limit) {
         // Over the cache limit: let the driver have it (cudaFree waits for
         // the device, so enqueued users finish first).
@@ -341,6 +378,102 @@ vc_status vc_cuda_pool_stats(size_t* cached_bytes, size_t* in_use_bytes, size_t*
     if (in_use_bytes) *in_use_bytes = pool.in_use_bytes;
     if (hits) *hits = pool.hits;
     if (misses) *misses = pool.misses;
+    VC_API_END
+}
+
+vc_status vc_cuda_graph_begin(void) {
+    VC_API_BEGIN
+    ensure_init();
+    State& s = state();
+    {
+        std::lock_guard<std::mutex> lock(s.pool.mutex);
+        if (s.pool.capturing) fail(VC_ERR_INVALID, "vc_cuda_graph_begin: a capture is already in progress");
+        s.pool.capturing = new GraphRecord();
+    }
+    const cudaError_t err = cudaStreamBeginCapture(s.stream, cudaStreamCaptureModeRelaxed);
+    if (err != cudaSuccess) {
+        std::lock_guard<std::mutex> lock(s.pool.mutex);
+        delete s.pool.capturing;
+        s.pool.capturing = nullptr;
+        check_cuda(err, "cudaStreamBeginCapture");
+    }
+    VC_API_END
+}
+
+vc_status vc_cuda_graph_end(void** graph) {
+    VC_API_BEGIN
+    ensure_init();
+    State& s = state();
+    GraphRecord* g = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(s.pool.mutex);
+        g = s.pool.capturing;
+        if (!g) fail(VC_ERR_INVALID, "vc_cuda_graph_end: no capture in progress");
+        s.pool.capturing = nullptr;
+        // blocks freed during the capture stay with the graph
+        for (auto& entry : g->capture_free)
+            for (void* p : entry.second) g->reserved.emplace_back(p, entry.first);
+        g->capture_free.clear();
+    }
+    cudaError_t err = cudaStreamEndCapture(s.stream, &g->graph);
+    if (err == cudaSuccess) err = cudaGraphInstantiate(&g->exec, g->graph, 0);
+    if (err == cudaSuccess) {
+        std::size_t nodes = 0;
+        if (cudaGraphGetNodes(g->graph, nullptr, &nodes) == cudaSuccess) g->kernels = nodes;
+    }
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        vc_cuda_graph_destroy(g);
+        check_cuda(err, "graph capture (an operation in the captured region synchronised or failed)");
+    }
+    if (!graph) {
+        vc_cuda_graph_destroy(g);
+        fail(VC_ERR_INVALID, "vc_cuda_graph_end: null output");
+    }
+    *graph = g;
+    VC_API_END
+}
+
+vc_status vc_cuda_graph_launch(void* graph) {
+    VC_API_BEGIN
+    ensure_init();
+    auto* g = static_cast<GraphRecord*>(graph);
+    if (!g || !g->exec) fail(VC_ERR_INVALID, "vc_cuda_graph_launch: not a captured graph");
+    VC_CUDA(cudaGraphLaunch(g->exec, state().stream));
+    VC_API_END
+}
+
+vc_status vc_cuda_graph_nodes(void* graph, size_t* nodes) {
+    VC_API_BEGIN
+    auto* g = static_cast<GraphRecord*>(graph);
+    if (!g || !nodes) fail(VC_ERR_INVALID, "vc_cuda_graph_nodes: null argument");
+    *nodes = g->kernels;
+    VC_API_END
+}
+
+vc_status vc_cuda_graph_destroy(void* graph) {
+    VC_API_BEGIN
+    auto* g = static_cast<GraphRecord*>(graph);
+    if (!g) return VC_OK;
+    State& s = state();
+    // replays already enqueued run before any later user of the blocks
+    // (one stream); the reserved blocks go back to the pool
+    if (g->exec) cudaGraphExecDestroy(g->exec);
+    if (g->graph) cudaGraphDestroy(g->graph);
+    {
+        // blocks still held by tensors lose the graph tag (freed normally
+        // later); the reserved ones return to the cache
+        std::lock_guard<std::mutex> lock(s.pool.mutex);
+        for (auto it = s.pool.owner.begin(); it != s.pool.owner.end();) {
+            if (it->second == g) it = s.pool.owner.erase(it);
+            else ++it;
+        }
+        for (const auto& entry : g->reserved) {
+            s.pool.free_blocks[entry.second].push_back(entry.first);
+            s.pool.cached_bytes += entry.second;
+        }
+    }
+    delete g;
     VC_API_END
 }
 

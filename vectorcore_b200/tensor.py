@@ -814,6 +814,27 @@ def cross_entropy(logits: Tensor, targets) -> Tensor:
     return out
 
 
+def bias_relu_sum(x: Tensor, b: Tensor) -> Tensor:
+    """relu(x + b).sum() for x [rows, cols] and a bias b [cols], fused: one
+    kernel forward, one backward (same values as the composed ops: the loss
+    and db within the sum tolerance, dx bit for bit)."""
+    _same_device(x, b)
+    if x.ndim != 2 or b.ndim != 1 or b._impl.shape[0] != x._impl.shape[1]:
+        raise ValueError(f"bias_relu_sum expects x [rows, cols] and b [cols], got {x.shape} and {b.shape}")
+    rows, cols = x._impl.shape
+    be = _be()
+    out = _out(be.bias_relu_sum(x._impl.storage, b._impl.storage, rows, cols), ())
+    saved_x, saved_b = SavedTensor(x), SavedTensor(b)
+
+    def backward(g: Tensor):
+        xs, bs = saved_x.unpack(), saved_b.unpack()
+        dx, db = be.bias_relu_sum_backward(xs._impl.storage, bs._impl.storage, g._impl.storage, rows, cols)
+        return [_out(dx, (rows, cols)), _out(db, (cols,))]
+
+    _attach(out, [x, b], backward)
+    return out
+
+
 # ---------------------------------------------------------------------------------------
 # matmul / transpose (src/ops.cpp:166-286) -- existing ops, correct not tuned
 # ---------------------------------------------------------------------------------------
