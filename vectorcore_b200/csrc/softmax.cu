@@ -79,24 +79,20 @@ struct RowArgs {
 
 // ---- row-sum helpers ----------------------------------------------------------
 // exp(x) for the terms of a row sum (x = logit - row max <= 0): 2^(x log2 e)
-// on the SFU's ex2.approx, with the product x * log2(e) carried in two
-// floats -- t = fl(x * L2E_HI), tl = (x * L2E_HI - t) + x * L2E_LO via FMA
-// (Dekker-style product splitting) -- and 2^tl applied to first order,
-// 2^t * (1 + tl ln 2). The error is ex2.approx's (relative below 2^-22) plus
-// about 1e-7 from the first-order step: a few float ulps of each term, far
-// inside the sum tolerance. Per-element outputs keep expf. x is clamped
-// (NaN-preserving) at -110, where 2^t is already 0.
-constexpr float kL2eHi = 0x1.715476p+0f;   // log2(e) rounded to float
-constexpr float kL2eLo = 0x1.4ae0c0p-26f;  // log2(e) - kL2eHi
-constexpr float kLn2 = 0x1.62e430p-1f;     // ln(2) rounded to float
+// on the SFU's ex2.approx. Rounding x * log2(e) to float perturbs a term by
+// at most |x| * 2^-24 * log2(e) * ln 2 relative, so the terms near the max
+// (which carry the sum) are within a few float ulps and the far ones, though
+// less accurate, are exponentially small: the row sum stays within about
+// 2e-7 of the reference's double sum of expf, far inside the 1e-5 tolerance.
+// Per-element outputs keep expf. x is clamped (NaN-preserving) at -110,
+// where 2^t is already 0 (and -inf logits give 0, not NaN).
+constexpr float kL2e = 0x1.715476p+0f;  // log2(e) rounded to float
 __device__ __forceinline__ float exp_sum_term(float x) {
     float xc;
     asm("max.NaN.f32 %0, %1, %2;" : "=f"(xc) : "f"(x), "f"(-110.0f));
-    const float t = xc * kL2eHi;
-    const float tl = __fmaf_rn(xc, kL2eLo, __fmaf_rn(xc, kL2eHi, -t));
     float e;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(t));
-    return __fmaf_rn(e, tl * kLn2, e);
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(xc * kL2e));
+    return e;
 }
 
 // Row sums accumulate per float4: the four terms in float ((x + y) + (z + w)),
@@ -498,6 +494,9 @@ template <int MODE> struct PipeTraits {
     static constexpr bool FWD = MODE == LSM_FWD || MODE == SM_FWD || MODE == CE_FWD;
     static constexpr bool STAGE_G = MODE == LSM_BWD || MODE == SM_BWD;
     static constexpr unsigned NBUF = STAGE_G ? 2u : 1u;
+    // resident CTAs per SM the register budget is sized for (each holds
+    // 64 KB of stages: three fit)
+    static constexpr unsigned MIN_CTAS = 3u;
 };
 
 __device__ __forceinline__ float warp_fmax(float v) {
@@ -514,11 +513,6 @@ __device__ __forceinline__ unsigned mapa_cluster(unsigned cta_addr, unsigned ran
     unsigned r;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(cta_addr), "r"(rank));
     return r;
-}
-__device__ __forceinline__ void st_async_b32(unsigned addr, unsigned v, unsigned bar) {
-    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(addr), "r"(v),
-                 "r"(bar)
-                 : "memory");
 }
 __device__ __forceinline__ void st_async_b64(unsigned addr, unsigned long long v, unsigned bar) {
     asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b64 [%0], %1, [%2];" ::"r"(addr), "l"(v),
@@ -540,21 +534,13 @@ __device__ __forceinline__ bool exchange(T v, T* slots, unsigned long long* bar,
     if ((threadIdx.x & 31) == 0) {
         const unsigned slot = smem_addr(slots + rank * kWarps + (threadIdx.x >> 5));
         const unsigned b = smem_addr(bar);
-        for (unsigned r = 0; r < C; ++r) {
-            if constexpr (sizeof(T) == 4) st_async_b32(mapa_cluster(slot, r), __float_as_uint(v), mapa_cluster(b, r));
-            else st_async_b64(mapa_cluster(slot, r), bits64(v), mapa_cluster(b, r));
-        }
+        for (unsigned r = 0; r < C; ++r) st_async_b64(mapa_cluster(slot, r), bits64(v), mapa_cluster(b, r));
     }
     bool good = ok;
     if (threadIdx.x == 0 && ok) good = mbar_wait_bounded(bar, parity, err);
     return __syncthreads_and(good) != 0;
 }
 
-__device__ __forceinline__ float fold_fmax(const float* slots, unsigned C) {
-    float t = -INFINITY;
-    for (unsigned i = threadIdx.x & 31; i < C * kWarps; i += 32) t = fmaxf(t, slots[i]);
-    return warp_fmax(t);
-}
 __device__ __forceinline__ unsigned long long fold_umin(const unsigned long long* slots, unsigned C) {
     unsigned long long t = ~0ull;
     for (unsigned i = threadIdx.x & 31; i < C * kWarps; i += 32) t = min(t, slots[i]);
@@ -567,14 +553,49 @@ __device__ __forceinline__ double fold_sum(const double* slots, unsigned C) {
 }
 __device__ __forceinline__ float4 neg4(float4 v) { return make_float4(-v.x, -v.y, -v.z, -v.w); }
 
+// The per-warp (max, sum of exp(x - max)) pairs of a row: one exchange of
+// 16-byte slots {double(m_w), s_w}.
+__device__ __forceinline__ void st_async_v2_b64(unsigned addr, unsigned long long a, unsigned long long b,
+                                                unsigned bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.b64 [%0], {%1, %2}, [%3];" ::"r"(addr),
+                 "l"(a), "l"(b), "r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ bool exchange_pair(float m, double s, double2* slots, unsigned long long* bar,
+                                              unsigned parity, unsigned C, unsigned rank, bool ok, unsigned* err) {
+    if (threadIdx.x == 0) mbar_expect_tx(bar, C * kWarps * static_cast<unsigned>(sizeof(double2)));
+    if ((threadIdx.x & 31) == 0) {
+        const unsigned slot = smem_addr(slots + rank * kWarps + (threadIdx.x >> 5));
+        const unsigned b = smem_addr(bar);
+        for (unsigned r = 0; r < C; ++r)
+            st_async_v2_b64(mapa_cluster(slot, r), bits64(static_cast<double>(m)), bits64(s), mapa_cluster(b, r));
+    }
+    bool good = ok;
+    if (threadIdx.x == 0 && ok) good = mbar_wait_bounded(bar, parity, err);
+    return __syncthreads_and(good) != 0;
+}
+// Row max m = max of the m_w (fmaxf skips NaN) and s = sum of s_w * exp(m_w - m)
+// in double, lane-parallel then a fixed xor tree. A slot with m_w = -inf
+// carries s_w = 0 (or NaN): its weight exp(-inf - m) is 0 and NaN survives.
+__device__ __forceinline__ void fold_pairs(const double2* slots, unsigned C, float& m, double& s) {
+    float mm = -INFINITY;
+    for (unsigned i = threadIdx.x & 31; i < C * kWarps; i += 32) mm = fmaxf(mm, static_cast<float>(slots[i].x));
+    mm = warp_fmax(mm);
+    double t = 0.0;
+    for (unsigned i = threadIdx.x & 31; i < C * kWarps; i += 32)
+        t += slots[i].y * static_cast<double>(expf(static_cast<float>(slots[i].x) - mm));
+    m = mm;
+    s = warp_sum(t);
+}
+
 template <int MODE>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, PipeTraits<MODE>::MIN_CTAS)
 row_pipe_kernel(const RowArgs a) {
     using T = PipeTraits<MODE>;
     extern __shared__ __align__(128) float smem[];
     __shared__ unsigned long long bar[2];        // stage copies
     __shared__ unsigned long long xbar[3][2];    // exchanges: max, first-zero index, sum
-    __shared__ float xs_max[2][kMaxCluster * kWarps];
+    __shared__ double2 xs_ms[2][kMaxCluster * kWarps];
     __shared__ unsigned long long xs_idx[2][kMaxCluster * kWarps];
     __shared__ double xs_sum[2][kMaxCluster * kWarps];
 
@@ -637,14 +658,38 @@ row_pipe_kernel(const RowArgs a) {
 
         if constexpr (T::FWD) {
             const float first = __ldg(a.x + row * a.L);
-            // ---- row max m: fmaxf skips NaN; then the scan's exact rules ----
+            // ---- per warp: its max m_w (fmaxf skips NaN) and s_w = sum of
+            // exp(x - m_w); ONE cluster exchange of the (m_w, s_w) pairs gives
+            // the row max m and s = sum of s_w * exp(m_w - m) ----
             float mloc = -INFINITY;
             for (unsigned j = threadIdx.x; j < n4; j += kThreads) {
                 const float4 v = ld_smem4(sx, j);
                 mloc = fmaxf(mloc, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
             }
-            ok = exchange(warp_fmax(mloc), xs_max[st], &xbar[0][st], par, C, rank, ok, a.err);
-            float m = fold_fmax(xs_max[st], C);
+            const float mw = warp_fmax(mloc);
+            double part = 0.0;
+            for (unsigned j = threadIdx.x; j < n4; j += kThreads) {
+                const float4 v = ld_smem4(sx, j);
+                part += quad_sum(make_float4(exp_sum_term(v.x - mw), exp_sum_term(v.y - mw), exp_sum_term(v.z - mw),
+                                             exp_sum_term(v.w - mw)));
+            }
+            double sw = warp_sum(part);
+            if (mw == -INFINITY) {
+                // no finite value among this warp's elements: they add 0 to
+                // the row sum, or NaN when one of them is NaN
+                bool nan = false;
+                for (unsigned j = threadIdx.x; j < n4; j += kThreads) {
+                    const float4 v = ld_smem4(sx, j);
+                    nan = nan || v.x != v.x || v.y != v.y || v.z != v.z || v.w != v.w;
+                }
+                sw = __any_sync(0xffffffffu, nan) ? static_cast<double>(__int_as_float(0x7fc00000)) : 0.0;
+            }
+            ok = exchange_pair(mw, sw, xs_ms[st], &xbar[0][st], par, C, rank, ok, a.err);
+            float m;
+            double s_row;
+            fold_pairs(xs_ms[st], C, m, s_row);
+            // a row of -inf only: the reference's x - m is NaN everywhere
+            if (m == -INFINITY) s_row = static_cast<double>(__int_as_float(0x7fc00000));
             if (first != first) {
                 m = first;  // the scan never leaves a NaN at index 0
             } else if (m == 0.0f) {
@@ -659,15 +704,7 @@ row_pipe_kernel(const RowArgs a) {
                 ++nz;
                 if (idx < a.L) m = __ldg(a.x + row * a.L + idx);
             }
-            // ---- s = float(sum of exp(x - m)) ----
-            double part = 0.0;
-            for (unsigned j = threadIdx.x; j < n4; j += kThreads) {
-                const float4 v = ld_smem4(sx, j);
-                part += quad_sum(make_float4(exp_sum_term(v.x - m), exp_sum_term(v.y - m), exp_sum_term(v.z - m),
-                                             exp_sum_term(v.w - m)));
-            }
-            ok = exchange(warp_sum(part), xs_sum[st], &xbar[2][st], par, C, rank, ok, a.err);
-            const float s = static_cast<float>(fold_sum(xs_sum[st], C));
+            const float s = static_cast<float>(s_row);
             const float l = logf(s);
             if (rank == 0 && threadIdx.x == 0) {
                 if (a.row_max) a.row_max[row] = m;
