@@ -28,8 +28,12 @@ constexpr unsigned kThreads = 256;
 constexpr unsigned kTicketForward = 0;        // ticket counter slots
 constexpr unsigned kTicketBackward = 1;
 constexpr unsigned kFwdPerThread = 4;         // forward: float4 groups per thread (in flight together)
-constexpr unsigned kBwdSegRows = 16;          // backward: rows per CTA
-constexpr unsigned kBwdColBlock = kThreads * 4;  // backward: columns per CTA (float4 lanes)
+// backward CTA: 64 float4 columns (256 floats) x 4 row groups x 4 rows
+constexpr unsigned kBwdLanes = 64;
+constexpr unsigned kBwdGroups = kThreads / kBwdLanes;
+constexpr unsigned kBwdRowsPerThread = 4;
+constexpr unsigned kBwdSegRows = kBwdGroups * kBwdRowsPerThread;
+constexpr unsigned kBwdColBlock = kBwdLanes * 4;
 
 __device__ __forceinline__ float relu_of(float h) { return h > 0.0f ? h : 0.0f; }
 
@@ -117,54 +121,70 @@ __device__ __forceinline__ double db_from_count(float g, unsigned long long coun
     return static_cast<double>(g) * static_cast<double>(count);
 }
 
-// Backward. grid = (column blocks, row segments). Thread t of column block cb
-// owns float4 column cb*256 + t (or columns cb*1024 + t + 256k) over the
-// CTA's rows: writes dx and counts its rows with h > 0; the counts go to
-// `counts` with integer atomics (exact in any order), and the last CTA
-// converts them to db and clears them.
+// Backward. grid = (column blocks of 256, row segments of 16). Thread
+// (lane, group) owns columns c0 + 4*lane .. +3 (or c0 + lane + 64k without
+// float4) over rows r0 + 4*group .. +3: loads them together, writes dx and
+// counts its rows with h > 0. The four groups' counts meet in shared memory
+// and go to `counts` with one integer atomic per column and CTA (exact in any
+// order); the last CTA converts them to db and clears them.
 template <bool VEC>
 __global__ void __launch_bounds__(kThreads)
 bias_relu_sum_bwd(const float* __restrict__ x, const float* __restrict__ b, const float* __restrict__ upstream,
                   unsigned long long rows, unsigned long long cols, float* __restrict__ dx, float* __restrict__ db,
                   double* __restrict__ db_d, unsigned* __restrict__ counts, unsigned* __restrict__ ticket) {
     __shared__ bool s_last;
+    __shared__ unsigned s_cnt[kBwdGroups][kBwdColBlock];
     const float g = __ldg(upstream) + 0.0f;  // broadcast_to(u): u + 0
-    const unsigned long long r0 = static_cast<unsigned long long>(blockIdx.y) * kBwdSegRows;
-    const unsigned long long r1 = min(rows, r0 + kBwdSegRows);
+    const unsigned lane = threadIdx.x % kBwdLanes, grp = threadIdx.x / kBwdLanes;
+    const unsigned long long r0 = static_cast<unsigned long long>(blockIdx.y) * kBwdSegRows + grp * kBwdRowsPerThread;
     const unsigned long long c0 = static_cast<unsigned long long>(blockIdx.x) * kBwdColBlock;
+    unsigned n[4] = {0, 0, 0, 0};
     if constexpr (VEC) {
-        const unsigned long long c = c0 + 4ull * threadIdx.x;
+        const unsigned long long c = c0 + 4ull * lane;
         if (c < cols) {
             const float4 bv = ldg4(b + c);
-            unsigned n0 = 0, n1 = 0, n2 = 0, n3 = 0;
-#pragma unroll 8
-            for (unsigned long long r = r0; r < r1; ++r) {
-                const float4 xv = ldg4(x + r * cols + c);
+            float4 xs[kBwdRowsPerThread];
+#pragma unroll
+            for (unsigned k = 0; k < kBwdRowsPerThread; ++k)
+                if (r0 + k < rows) xs[k] = ldg4(x + (r0 + k) * cols + c);
+#pragma unroll
+            for (unsigned k = 0; k < kBwdRowsPerThread; ++k) {
+                if (r0 + k >= rows) break;
+                const float4 xv = xs[k];
                 const bool p0 = (xv.x + bv.x) > 0.0f, p1 = (xv.y + bv.y) > 0.0f;
                 const bool p2 = (xv.z + bv.z) > 0.0f, p3 = (xv.w + bv.w) > 0.0f;
-                st4_stream(dx + r * cols + c, make_float4(g * (p0 ? 1.0f : 0.0f), g * (p1 ? 1.0f : 0.0f),
-                                                          g * (p2 ? 1.0f : 0.0f), g * (p3 ? 1.0f : 0.0f)));
-                n0 += p0;
-                n1 += p1;
-                n2 += p2;
-                n3 += p3;
+                st4_stream(dx + (r0 + k) * cols + c, make_float4(g * (p0 ? 1.0f : 0.0f), g * (p1 ? 1.0f : 0.0f),
+                                                                 g * (p2 ? 1.0f : 0.0f), g * (p3 ? 1.0f : 0.0f)));
+                n[0] += p0;
+                n[1] += p1;
+                n[2] += p2;
+                n[3] += p3;
             }
-            if (n0) atomicAdd(counts + c, n0);
-            if (n1) atomicAdd(counts + c + 1, n1);
-            if (n2) atomicAdd(counts + c + 2, n2);
-            if (n3) atomicAdd(counts + c + 3, n3);
         }
+#pragma unroll
+        for (unsigned j = 0; j < 4; ++j) s_cnt[grp][4 * lane + j] = n[j];
     } else {
-        for (unsigned long long c = c0 + threadIdx.x; c < min(cols, c0 + kBwdColBlock); c += kThreads) {
-            const float bv = __ldg(b + c);
-            unsigned n = 0;
-            for (unsigned long long r = r0; r < r1; ++r) {
-                const bool p = (__ldg(x + r * cols + c) + bv) > 0.0f;
-                dx[r * cols + c] = g * (p ? 1.0f : 0.0f);
-                n += p;
+#pragma unroll
+        for (unsigned j = 0; j < 4; ++j) {
+            const unsigned long long c = c0 + lane + kBwdLanes * j;
+            if (c < cols) {
+                const float bv = __ldg(b + c);
+                for (unsigned k = 0; k < kBwdRowsPerThread && r0 + k < rows; ++k) {
+                    const bool p = (__ldg(x + (r0 + k) * cols + c) + bv) > 0.0f;
+                    dx[(r0 + k) * cols + c] = g * (p ? 1.0f : 0.0f);
+                    n[j] += p;
+                }
             }
-            if (n) atomicAdd(counts + c, n);
+            s_cnt[grp][lane + kBwdLanes * j] = n[j];
         }
+    }
+    __syncthreads();
+    for (unsigned col = threadIdx.x; col < kBwdColBlock; col += kThreads) {
+        const unsigned long long c = c0 + col;
+        unsigned t = 0;
+#pragma unroll
+        for (unsigned q = 0; q < kBwdGroups; ++q) t += s_cnt[q][col];
+        if (t && c < cols) atomicAdd(counts + c, t);
     }
     if (!arrive_last(ticket, gridDim.x * gridDim.y, &s_last)) return;
     for (unsigned long long c = threadIdx.x; c < cols; c += kThreads) {

@@ -174,22 +174,39 @@ reduce_col_kernel(const float* __restrict__ g, const float* __restrict__ p, cons
                 acc[3] += static_cast<double>(v.w);
             }
         };
+        // a group of four positions added in float ((a + b) + (c + d)), the
+        // group in double: one float->double conversion per four terms; a
+        // group that overflows float is added term by term in double
+        auto accumulate_quad = [&](float4 a, float4 b, float4 c, float4 e) {
+            auto q = [](double& acc_, float w, float x, float y, float z) {
+                const float t = (w + x) + (y + z);
+                if (isfinite(t)) acc_ += static_cast<double>(t);
+                else acc_ += ((static_cast<double>(w) + static_cast<double>(x)) + static_cast<double>(y)) +
+                             static_cast<double>(z);
+            };
+            q(acc[0], a.x, b.x, c.x, e.x);
+            if constexpr (VEC) {
+                q(acc[1], a.y, b.y, c.y, e.y);
+                q(acc[2], a.z, b.z, c.z, e.z);
+                q(acc[3], a.w, b.w, c.w, e.w);
+            }
+        };
         unsigned long long r = r0;
-        // four reduced positions in flight, accumulated in order
-        for (; r + 3 < r1; r += 4) {
-            long long o0[3] = {off[0], off[1], off[2]};
-            advance();
-            long long o1[3] = {off[0], off[1], off[2]};
-            advance();
-            long long o2[3] = {off[0], off[1], off[2]};
-            advance();
-            long long o3[3] = {off[0], off[1], off[2]};
-            advance();
-            const float4 v0 = fetch(o0), v1 = fetch(o1), v2 = fetch(o2), v3 = fetch(o3);
-            accumulate(v0);
-            accumulate(v1);
-            accumulate(v2);
-            accumulate(v3);
+        // eight reduced positions in flight, accumulated in order
+        for (; r + 7 < r1; r += 8) {
+            long long o[8][3];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                o[k][0] = off[0];
+                o[k][1] = off[1];
+                o[k][2] = off[2];
+                advance();
+            }
+            float4 v[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) v[k] = fetch(o[k]);
+            accumulate_quad(v[0], v[1], v[2], v[3]);
+            accumulate_quad(v[4], v[5], v[6], v[7]);
         }
         for (; r < r1; ++r) {
             accumulate(fetch(off));
@@ -219,8 +236,17 @@ reduce_col_finish(const double* __restrict__ partial, unsigned S, unsigned long 
     const unsigned long long stride = static_cast<unsigned long long>(gridDim.x) * blockDim.x;
     for (unsigned long long o = static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x; o < count;
          o += stride) {
+        // eight segment partials in flight, added in segment order
         double acc = 0.0;
-        for (unsigned s = 0; s < S; ++s) acc += partial[static_cast<unsigned long long>(s) * count + o];
+        unsigned s = 0;
+        for (; s + 8 <= S; s += 8) {
+            double v[8];
+#pragma unroll
+            for (unsigned k = 0; k < 8; ++k) v[k] = __ldg(partial + static_cast<unsigned long long>(s + k) * count + o);
+#pragma unroll
+            for (unsigned k = 0; k < 8; ++k) acc += v[k];
+        }
+        for (; s < S; ++s) acc += __ldg(partial + static_cast<unsigned long long>(s) * count + o);
         if (out_d) out_d[o] = acc;
         else out[o] = round_out(acc, divisor);
     }
@@ -1191,12 +1217,12 @@ max_col_kernel(const float* __restrict__ in, unsigned long long outer, unsigned 
             else return make_float4(__ldg(x + a * inner), 0.f, 0.f, 0.f);
         };
         unsigned long long a = a0;
-        for (; a + 3 < a1; a += 4) {
-            const float4 v0 = load(a), v1 = load(a + 1), v2 = load(a + 2), v3 = load(a + 3);
-            take(v0, a);
-            take(v1, a + 1);
-            take(v2, a + 2);
-            take(v3, a + 3);
+        for (; a + 7 < a1; a += 8) {
+            float4 v[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) v[k] = load(a + k);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) take(v[k], a + k);
         }
         for (; a < a1; ++a) take(load(a), a);
 #pragma unroll
@@ -1216,8 +1242,18 @@ max_col_finish(const float* __restrict__ in, unsigned long long outer, unsigned 
     const unsigned long long stride = static_cast<unsigned long long>(gridDim.x) * blockDim.x;
     for (unsigned long long k = static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x; k < count;
          k += stride) {
+        // eight segment candidates in flight, combined in segment order
         MaxCand c{0.0f, -1};
-        for (unsigned s = 0; s < S; ++s) c = max_combine(c, MaxCand{pv[s * count + k], pi[s * count + k]});
+        unsigned s = 0;
+        for (; s + 8 <= S; s += 8) {
+            MaxCand v[8];
+#pragma unroll
+            for (unsigned q = 0; q < 8; ++q)
+                v[q] = MaxCand{__ldg(pv + (s + q) * count + k), __ldg(pi + (s + q) * count + k)};
+#pragma unroll
+            for (unsigned q = 0; q < 8; ++q) c = max_combine(c, v[q]);
+        }
+        for (; s < S; ++s) c = max_combine(c, MaxCand{pv[s * count + k], pi[s * count + k]});
         const unsigned long long ob = k / inner, i = k - ob * inner;
         max_finish_write(c, in[ob * length * inner + i], o, k);
     }
