@@ -174,23 +174,6 @@ reduce_col_kernel(const float* __restrict__ g, const float* __restrict__ p, cons
                 acc[3] += static_cast<double>(v.w);
             }
         };
-        // a group of four positions added in float ((a + b) + (c + d)), the
-        // group in double: one float->double conversion per four terms; a
-        // group that overflows float is added term by term in double
-        auto accumulate_quad = [&](float4 a, float4 b, float4 c, float4 e) {
-            auto q = [](double& acc_, float w, float x, float y, float z) {
-                const float t = (w + x) + (y + z);
-                if (isfinite(t)) acc_ += static_cast<double>(t);
-                else acc_ += ((static_cast<double>(w) + static_cast<double>(x)) + static_cast<double>(y)) +
-                             static_cast<double>(z);
-            };
-            q(acc[0], a.x, b.x, c.x, e.x);
-            if constexpr (VEC) {
-                q(acc[1], a.y, b.y, c.y, e.y);
-                q(acc[2], a.z, b.z, c.z, e.z);
-                q(acc[3], a.w, b.w, c.w, e.w);
-            }
-        };
         unsigned long long r = r0;
         // eight reduced positions in flight, accumulated in order
         for (; r + 7 < r1; r += 8) {
@@ -205,8 +188,8 @@ reduce_col_kernel(const float* __restrict__ g, const float* __restrict__ p, cons
             float4 v[8];
 #pragma unroll
             for (int k = 0; k < 8; ++k) v[k] = fetch(o[k]);
-            accumulate_quad(v[0], v[1], v[2], v[3]);
-            accumulate_quad(v[4], v[5], v[6], v[7]);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) accumulate(v[k]);
         }
         for (; r < r1; ++r) {
             accumulate(fetch(off));
