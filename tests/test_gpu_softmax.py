@@ -117,6 +117,44 @@ def test_cross_entropy(backend, port):
             assert_rel(backend.download(dx).reshape(shape), rdx, RTOL, f"dlogits {shape} u={u}")
 
 
+@pytest.mark.parametrize("length", [4, 12, 132, 1024, 32000])
+def test_cross_entropy_edge_rows_among_many(backend, port, length):
+    """The cross-entropy row statistics under the scan's special cases (a
+    zero maximum whose first zero is -0.0, NaN at index 0, NaN elsewhere,
+    -inf, +-1000), for rows shorter than a warp's first pass (4, 12 values)
+    and longer; the loss of the rows without NaN."""
+    rows = 3000 if length <= 1024 else 400
+    rng = np.random.default_rng(length + 1)
+    x = rng.normal(0, 2, size=(rows, length)).astype(np.float32)
+    x[5] = 0.0
+    x[5, : length // 3] = -5.0
+    x[5, length // 3] = -0.0
+    x[6] = -0.0
+    x[6, length - 1] = 0.0
+    x[rows - 1, ::3] = -np.inf
+    x[rows - 2, 1] = 1000.0
+    x[rows - 2, length - 2] = -1000.0
+    x[rows - 3] = 0.0
+    tg = rng.integers(0, length, rows).astype(np.int64)
+    tg[rows - 1] = 1  # a finite logit: the loss stays finite
+    dtg = dev(backend, tg)
+    loss, _, _, _ = backend.cross_entropy(dev(backend, x), dtg, rows, length)
+    ref_loss, _ = port.cross_entropy(x, tg, 1.0)
+    assert_rel(backend.download(loss), np.array([ref_loss]), RTOL, f"loss {length}")
+    x[7, 0] = np.nan
+    x[rows // 2, length - 1] = np.nan
+    with np.errstate(invalid="ignore"):
+        _, m, s, _ = backend.cross_entropy(dev(backend, x), dtg, rows, length)
+        _, pm, ps = port.log_softmax(x, -1, stats=True)
+    got_m, got_s = backend.download(m), backend.download(s)
+    same = (got_m.view(np.uint32) == pm.view(np.uint32)) | (np.isnan(got_m) & np.isnan(pm))
+    assert same.all(), np.flatnonzero(~same)[:10]
+    assert got_m.view(np.uint32)[5] == np.float32(-0.0).view(np.uint32)
+    assert np.array_equal(np.isnan(got_s), np.isnan(ps)), np.flatnonzero(np.isnan(got_s) != np.isnan(ps))[:10]
+    ok = ~np.isnan(ps)
+    np.testing.assert_allclose(got_s[ok], ps[ok], rtol=2e-6, atol=0)
+
+
 def test_cross_entropy_known_answers(backend, golden):
     lg = np.zeros((2, 2), np.float32)
     loss, m, s, _ = backend.cross_entropy(dev(backend, lg), dev(backend, np.array([0, 1], np.int64)), 2, 2)

@@ -771,6 +771,103 @@ row_pipe_kernel(const RowArgs a) {
     cluster.sync();
 }
 
+// ---------------------------------------------------------------------------
+// Cross-entropy forward, aligned rows: one warp per row streams it ONCE from
+// HBM (float4, four loads per lane in flight) with an online max / sum --
+// no staging, no cluster exchange: CE writes nothing per element, so only the
+// row statistics and x[target] are needed. Per 16-value group: if the
+// group's max exceeds the lane's running max m, s *= exp(m - max) and m =
+// max; then the group's exp(x - m) terms are added (quads in float, then
+// double). Lanes fold as sum of s_l * exp(m_l - m) in a fixed xor tree.
+// NaN anywhere makes s NaN; a row without a finite value makes s NaN (the
+// reference's x - m is NaN); m follows the scan's rules (NaN at index 0, the
+// first zero for a zero maximum), found with warp ballots.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float fmax4(float4 v) { return fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)); }
+__device__ __forceinline__ bool has_nan4(float4 v) { return v.x != v.x || v.y != v.y || v.z != v.z || v.w != v.w; }
+
+__global__ void __launch_bounds__(kThreads)
+ce_rows_kernel(const RowArgs a) {
+    const unsigned lane = threadIdx.x & 31;
+    const unsigned long long nwarps = (static_cast<unsigned long long>(gridDim.x) * blockDim.x) >> 5;
+    const unsigned long long L4 = a.L / 4;
+    for (unsigned long long row = (static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+         row < a.rows; row += nwarps) {
+        const float4* xr = reinterpret_cast<const float4*>(a.x + row * a.L);
+        float m = -INFINITY;
+        double s = 0.0;
+        bool nan_seen = false;
+        auto take = [&](const float4* v, int count) {
+            float mx = -INFINITY;
+            for (int k = 0; k < count; ++k) mx = fmaxf(mx, fmax4(v[k]));
+            if (mx > m) {  // NaN never compares greater
+                if (m != -INFINITY) s *= static_cast<double>(expf(m - mx));
+                m = mx;
+            }
+            if (m == -INFINITY) {
+                for (int k = 0; k < count; ++k) nan_seen = nan_seen || has_nan4(v[k]);
+            } else {
+                for (int k = 0; k < count; ++k)
+                    s += quad_sum(make_float4(exp_sum_term(v[k].x - m), exp_sum_term(v[k].y - m),
+                                              exp_sum_term(v[k].z - m), exp_sum_term(v[k].w - m)));
+            }
+        };
+        unsigned long long j = lane;
+        for (; j + 96 < L4; j += 128) {
+            float4 v[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) v[k] = __ldcs(xr + j + 32 * k);
+            take(v, 4);
+        }
+        for (; j < L4; j += 32) {
+            const float4 v = __ldcs(xr + j);
+            take(&v, 1);
+        }
+        // fold the lanes: m = max of m_l; s = sum of s_l * exp(m_l - m)
+        const float mrow = warp_fmax(m);
+        double t = m == -INFINITY ? (nan_seen ? static_cast<double>(__int_as_float(0x7fc00000)) : 0.0)
+                                  : s * static_cast<double>(expf(m - mrow));
+        t = warp_sum(t);
+        if (mrow == -INFINITY || __any_sync(0xffffffffu, nan_seen)) t = static_cast<double>(__int_as_float(0x7fc00000));
+        float mm = mrow;
+        const float first = __ldg(a.x + row * a.L);
+        if (first != first) {
+            mm = first;
+        } else if (mm == 0.0f) {
+            // the first zero of the row decides the sign of a zero maximum
+            for (unsigned long long q0 = 0; q0 < L4; q0 += 32) {  // warp-uniform trip count
+                const unsigned long long q = q0 + lane;
+                int pos = -1;
+                if (q < L4) {
+                    const float4 v = __ldg(xr + q);
+                    pos = v.x == 0.0f ? 0 : (v.y == 0.0f ? 1 : (v.z == 0.0f ? 2 : (v.w == 0.0f ? 3 : -1)));
+                }
+                const unsigned hit = __ballot_sync(0xffffffffu, pos >= 0);
+                if (hit) {
+                    const int src = __ffs(hit) - 1;
+                    const int p = __shfl_sync(0xffffffffu, pos, src);
+                    const unsigned long long qq = q0 + src;
+                    mm = __ldg(a.x + row * a.L + qq * 4 + p);
+                    break;
+                }
+            }
+        }
+        const float sf = static_cast<float>(t);
+        const float l = logf(sf);
+        if (lane == 0) {
+            if (a.row_max) a.row_max[row] = mm;
+            if (a.row_sum) a.row_sum[row] = sf;
+            const long long tg = __ldg(a.targets + row);
+            if (tg < 0 || static_cast<unsigned long long>(tg) >= a.L) {
+                atomicOr(a.err, kErrBadTarget);
+                a.row_term[row] = 0.0f;
+            } else {
+                a.row_term[row] = (__ldg(a.x + row * a.L + tg) - mm) - l;
+            }
+        }
+    }
+}
+
 template <int MODE, bool BULK>
 static void launch_rows_mode(const RowArgs& a, unsigned C, std::size_t smem) {
     static bool configured = false;
@@ -858,6 +955,14 @@ static void launch_family(RowArgs a, std::size_t outer, std::size_t length, std:
         a.rows = outer;
         const bool aligned = length % 4 == 0 && aligned16(a.x) && (!STAGE_G || aligned16(a.g)) &&
                              (!a.y || aligned16(a.y));
+        if (MODE == CE_FWD && length % 4 == 0 && aligned16(a.x)) {
+            const unsigned long long warps_per_cta = kThreads / 32;
+            const unsigned long long ctas = std::min<unsigned long long>(
+                (outer + warps_per_cta - 1) / warps_per_cta, static_cast<unsigned long long>(sm_count()) * 8 * 16);
+            ce_rows_kernel<<<static_cast<unsigned>(ctas), kThreads, 0, stream()>>>(a);
+            check_launch("cross_entropy_rows");
+            return;
+        }
         if (aligned) {
             constexpr unsigned NB = PipeTraits<MODE>::NBUF;
             unsigned C = 1;

@@ -124,11 +124,10 @@ __device__ __forceinline__ void st4_stream(float* p, float4 v) { __stcs(reinterp
 
 // ---------------------------------------------------------------------------
 // mbarrier helpers for bulk copies (TMA). Every wait is bounded: after
-// kWaitSpins polls it sets kErrWaitTimeout in the device error word and gives
+// kWaitPolls polls it sets kErrWaitTimeout in the device error word and gives
 // up, so a lost completion surfaces as an error at the next sync instead of a
 // hung kernel.
 // ---------------------------------------------------------------------------
-constexpr long long kWaitSpins = 1ll << 24;
 
 __device__ __forceinline__ unsigned smem_addr(const void* p) {
     return static_cast<unsigned>(__cvta_generic_to_shared(p));
@@ -148,19 +147,25 @@ __device__ __forceinline__ void mbar_expect_tx(unsigned long long* bar, unsigned
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
                  : "memory");
 }
+// One poll. The thread may sleep in it for up to kWaitHintNs (or until the
+// phase completes) instead of spinning, so a waiting warp issues few
+// instructions.
+constexpr unsigned kWaitHintNs = 2000;
 __device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned parity) {
     unsigned ok;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
-        : "r"(smem_addr(bar)), "r"(parity)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(kWaitHintNs)
         : "memory");
     return ok != 0;
 }
-// Wait for phase `parity` with an iteration limit; false (and the device
-// error bit) when it gave up.
+// Wait for phase `parity` with an iteration limit (at most kWaitPolls polls
+// of up to kWaitHintNs each, a few seconds); false (and the device error bit)
+// when it gave up.
+constexpr long long kWaitPolls = 1ll << 21;
 __device__ __forceinline__ bool mbar_wait_bounded(unsigned long long* bar, unsigned parity, unsigned* err) {
-    for (long long i = 0; i < kWaitSpins; ++i)
+    for (long long i = 0; i < kWaitPolls; ++i)
         if (mbar_try_wait(bar, parity)) return true;
     atomicOr(err, kErrWaitTimeout);
     return false;
