@@ -6,15 +6,21 @@
 // cross-entropy (src/ops.cpp:378-388, src/nn.cpp:31-53). Here each is ONE
 // pass over HBM: read x (and g) once, write the result once.
 //
-// Rows (reduction over the last axis): one thread-block cluster of C CTAs per
-// row, C in {1, 2, 4, 8} chosen so a CTA's slice of the row is at most 8K
-// floats (32 KB) -- small enough for several CTAs per SM so one CTA's loads
-// overlap another's arithmetic. Each CTA stages its slice in shared memory
-// with one TMA bulk copy of its own slice (cp.async.bulk into its own shared
-// memory, completion on an mbarrier), reduces it, and the C partials are exchanged through
-// distributed shared memory and combined in rank order, so every CTA of the
-// cluster derives the same row statistics. Other axes (and rows too long for
-// a cluster) take a column kernel that walks the axis in global memory.
+// Rows (reduction over the last axis), by row length:
+//  * aligned rows up to 32K floats: a group of warps per row reads the row
+//    from HBM once into registers, combines its statistics in shared memory
+//    and re-reads the row from L2 for the output (row_reread_kernel);
+//    cross-entropy's forward writes nothing per element and streams each
+//    row once, a warp per row (ce_rows_kernel);
+//  * longer aligned rows: one thread-block cluster of C CTAs per row, C in
+//    {1, 2, 4, 8}; each CTA stages its slice in shared memory with TMA bulk
+//    copies (cp.async.bulk, completion on an mbarrier, the next row in
+//    flight), and the partials are exchanged through distributed shared
+//    memory and combined in rank order, so every CTA of the cluster derives
+//    the same row statistics (row_pipe_kernel); unaligned rows take the
+//    one-shot cluster kernel with plain loads (row_kernel).
+// Other axes (and rows too long for a cluster) take a column kernel that
+// walks the axis in global memory.
 //
 // The arithmetic is the reference's, operation by operation:
 //   m  = max(x) with the scan semantics of cpu::reduce_axis,
@@ -868,6 +874,242 @@ ce_rows_kernel(const RowArgs a) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// Softmax family on aligned rows of up to kRereadMaxL floats, re-read
+// design: a group of W warps (W a power of two, 1..16) owns a row.
+//   pass 1 streams the row from HBM (four float4 loads per thread in flight)
+//          with an L2 evict_last policy and reduces it: forward, an online
+//          (max, sum of exp) per lane, rescaled when the lane's max grows;
+//          backward, the double sum the chain needs;
+//   the warps of the group combine their results through shared memory
+//          (one CTA barrier per row, slots double-buffered by iteration);
+//   pass 2 re-reads the row, now an L2 hit, with an evict_first policy and
+//          writes the output once.
+// No cluster lockstep and no shared-memory staging: the loads in flight are
+// bounded by registers, not by stage buffers. A CTA holds at most one row per
+// group, so the rows in flight (two 16-warp CTAs per SM) take a fraction of
+// the 126 MB L2 and HBM sees each input byte once. The per-element arithmetic
+// is the pipelined kernel's.
+// ---------------------------------------------------------------------------
+constexpr unsigned kRThreads = 512;
+constexpr unsigned kRWarps = kRThreads / 32;
+constexpr unsigned long long kRereadMaxL = 32768;
+
+__device__ __forceinline__ unsigned long long policy_evict_last() {
+    unsigned long long p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ unsigned long long policy_evict_first() {
+    unsigned long long p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+// Read-only float4 load with an L2 cache policy; not allocated in L1.
+__device__ __forceinline__ float4 ld4_hint(const float4* p, unsigned long long policy) {
+    float4 v;
+    asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
+        : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+        : "l"(p), "l"(policy));
+    return v;
+}
+
+// The first zero of a row (whose maximum is zero) decides the maximum's
+// sign: one warp scans the row with ballots (warp-uniform trip count).
+__device__ __forceinline__ float first_zero(const float* row, unsigned long long L4, unsigned lane) {
+    const float4* r4 = reinterpret_cast<const float4*>(row);
+    for (unsigned long long q0 = 0; q0 < L4; q0 += 32) {
+        const unsigned long long q = q0 + lane;
+        int pos = -1;
+        if (q < L4) {
+            const float4 v = __ldg(r4 + q);
+            pos = v.x == 0.0f ? 0 : (v.y == 0.0f ? 1 : (v.z == 0.0f ? 2 : (v.w == 0.0f ? 3 : -1)));
+        }
+        const unsigned hit = __ballot_sync(0xffffffffu, pos >= 0);
+        if (hit) {
+            const int src = __ffs(hit) - 1;
+            const int p = __shfl_sync(0xffffffffu, pos, src);
+            return __ldg(row + (q0 + src) * 4 + p);
+        }
+    }
+    return 0.0f;  // not reached: the caller saw a zero maximum
+}
+
+// Depth of a pass: float4 loads per thread per array in flight (one array
+// forward, x and g together backward).
+template <int MODE> __host__ __device__ constexpr unsigned reread_depth() {
+    return (MODE == LSM_FWD || MODE == SM_FWD) ? 8u : 4u;
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kRThreads, 2)
+row_reread_kernel(const RowArgs a, unsigned wlog2) {
+    constexpr bool FWD = MODE == LSM_FWD || MODE == SM_FWD;
+    constexpr unsigned D = reread_depth<MODE>();
+    __shared__ double2 slots[2][kRWarps];
+    const unsigned warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const unsigned W = 1u << wlog2;
+    const unsigned G = kRWarps >> wlog2;  // rows per CTA iteration
+    const unsigned grp = warp >> wlog2;
+    const unsigned gt = ((warp & (W - 1)) << 5) | lane, GT = W << 5;
+    const unsigned L4 = static_cast<unsigned>(a.L / 4);  // at most kRereadMaxL / 4
+    const unsigned long long keep = policy_evict_last(), drop = policy_evict_first();
+    const double qnan = static_cast<double>(__int_as_float(0x7fc00000));
+
+    // Every pass walks the row in rounds of D float4 per thread, all D loads
+    // of a round issued before any is used; in the last round the loads past
+    // the row's end re-read its last float4 and their values go unused.
+    unsigned it = 0;
+    for (unsigned long long base = static_cast<unsigned long long>(blockIdx.x) * G; base < a.rows;
+         base += static_cast<unsigned long long>(gridDim.x) * G, ++it) {
+        const unsigned long long row = base + grp;
+        const bool active = row < a.rows;
+        const float4* xr = reinterpret_cast<const float4*>(a.x + row * a.L);
+        const float4* gr = reinterpret_cast<const float4*>(a.g + row * a.L);
+        float4* yr = reinterpret_cast<float4*>(a.y + row * a.L);
+        double2* sl = slots[it & 1u];
+
+        // ---------------- pass 1 ----------------
+        if constexpr (FWD) {
+            float m = -INFINITY;
+            double s = 0.0;
+            bool nan_seen = false;
+            auto take = [&](const float4& v) {
+                const float mx = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
+                if (mx > m) {  // NaN never compares greater
+                    if (m != -INFINITY) s *= static_cast<double>(expf(m - mx));
+                    m = mx;
+                }
+                if (m == -INFINITY)
+                    nan_seen = nan_seen || v.x != v.x || v.y != v.y || v.z != v.z || v.w != v.w;
+                else
+                    s += quad_sum(make_float4(exp_sum_term(v.x - m), exp_sum_term(v.y - m), exp_sum_term(v.z - m),
+                                              exp_sum_term(v.w - m)));
+            };
+            if (active) {
+                for (unsigned j = gt; j < L4; j += D * GT) {
+                    float4 v[D];
+#pragma unroll
+                    for (unsigned k = 0; k < D; ++k) v[k] = ld4_hint(xr + min(j + k * GT, L4 - 1), keep);
+#pragma unroll
+                    for (unsigned k = 0; k < D; ++k)
+                        if (j + k * GT < L4) take(v[k]);
+                }
+            }
+            const float mw = warp_fmax(m);
+            double t = m == -INFINITY ? (nan_seen ? qnan : 0.0) : s * static_cast<double>(expf(m - mw));
+            t = warp_sum(t);
+            if (__any_sync(0xffffffffu, nan_seen)) t = qnan;
+            if (lane == 0) sl[warp] = make_double2(static_cast<double>(mw), t);
+        } else {
+            double part = 0.0;
+            if (active) {
+                const float m = MODE == SM_BWD ? __ldg(a.row_max + row) : 0.0f;
+                const float l = MODE == SM_BWD ? logf(__ldg(a.row_sum + row)) : 0.0f;
+                for (unsigned j = gt; j < L4; j += D * GT) {
+                    float4 g[D], x[D];
+#pragma unroll
+                    for (unsigned k = 0; k < D; ++k) {
+                        const unsigned jk = min(j + k * GT, L4 - 1);
+                        g[k] = ld4_hint(gr + jk, keep);
+                        if constexpr (MODE == SM_BWD) x[k] = ld4_hint(xr + jk, keep);
+                    }
+#pragma unroll
+                    for (unsigned k = 0; k < D; ++k)
+                        if (j + k * GT < L4) {
+                            if constexpr (MODE == LSM_BWD) {
+                                part += quad_sum(neg4(g[k]));
+                            } else {
+                                const float4 gv = g[k], xv = x[k];
+                                part += quad_sum(make_float4(-(gv.x * expf((xv.x - m) - l)), -(gv.y * expf((xv.y - m) - l)),
+                                                             -(gv.z * expf((xv.z - m) - l)), -(gv.w * expf((xv.w - m) - l))));
+                            }
+                        }
+                }
+            }
+            part = warp_sum(part);
+            if (lane == 0) sl[warp] = make_double2(part, 0.0);
+        }
+        __syncthreads();
+        if (!active) continue;  // the barrier above is the only one of an iteration
+
+        // ---------------- combine the group's warps (same order in each) ----------------
+        const double2* gs = sl + (grp << wlog2);
+        if constexpr (FWD) {
+            float mm = lane < W ? static_cast<float>(gs[lane].x) : -INFINITY;
+            mm = warp_fmax(mm);
+            double t = lane < W ? gs[lane].y * static_cast<double>(expf(static_cast<float>(gs[lane].x) - mm)) : 0.0;
+            double s_row = warp_sum(t);
+            // a row of -inf only: the reference's x - m is NaN everywhere
+            if (mm == -INFINITY) s_row = qnan;
+            float m = mm;
+            const float first = __ldg(a.x + row * a.L);
+            if (first != first) m = first;  // the scan never leaves a NaN at index 0
+            else if (m == 0.0f) m = first_zero(a.x + row * a.L, L4, lane);
+            const float s = static_cast<float>(s_row);
+            const float l = logf(s);
+            if (gt == 0) {
+                if (a.row_max) a.row_max[row] = m;
+                if (a.row_sum) a.row_sum[row] = s;
+            }
+            auto f = [&](float v) {
+                const float ls = (v - m) - l;
+                return MODE == SM_FWD ? expf(ls) : ls;
+            };
+            // ---------------- pass 2 ----------------
+            for (unsigned j = gt; j < L4; j += D * GT) {
+                float4 v[D];
+#pragma unroll
+                for (unsigned k = 0; k < D; ++k) v[k] = ld4_hint(xr + min(j + k * GT, L4 - 1), drop);
+#pragma unroll
+                for (unsigned k = 0; k < D; ++k)
+                    if (j + k * GT < L4)
+                        st4_stream(reinterpret_cast<float*>(yr + j + k * GT),
+                                   make_float4(f(v[k].x), f(v[k].y), f(v[k].z), f(v[k].w)));
+            }
+        } else {
+            const float m = __ldg(a.row_max + row), s = __ldg(a.row_sum + row);
+            const float l = MODE == SM_BWD ? logf(s) : 0.0f;
+            const float dl = static_cast<float>(warp_sum(lane < W ? gs[lane].x : 0.0));
+            const float de = (dl / s) + 0.0f;
+            // LSM_BWD: dx = g + de * expf(x - m)
+            // SM_BWD:  dx = gy + de * expf(x - m), gy = g * expf((x - m) - l)
+            auto f = [&](float g, float x) {
+                const float gy = MODE == SM_BWD ? g * expf((x - m) - l) : g;
+                return gy + de * expf(x - m);
+            };
+            // ---------------- pass 2 ----------------
+            for (unsigned j = gt; j < L4; j += D * GT) {
+                float4 g[D], x[D];
+#pragma unroll
+                for (unsigned k = 0; k < D; ++k) {
+                    const unsigned jk = min(j + k * GT, L4 - 1);
+                    g[k] = ld4_hint(gr + jk, drop);
+                    x[k] = MODE == SM_BWD ? ld4_hint(xr + jk, drop) : ld4_stream(reinterpret_cast<const float*>(xr + jk));
+                }
+#pragma unroll
+                for (unsigned k = 0; k < D; ++k)
+                    if (j + k * GT < L4)
+                        st4_stream(reinterpret_cast<float*>(yr + j + k * GT),
+                                   make_float4(f(g[k].x, x[k].x), f(g[k].y, x[k].y), f(g[k].z, x[k].z),
+                                               f(g[k].w, x[k].w)));
+            }
+        }
+    }
+}
+
+template <int MODE>
+static void launch_rows_reread(const RowArgs& a) {
+    const unsigned long long L4 = a.L / 4;
+    unsigned wlog2 = 0;
+    while (wlog2 < 4 && L4 > (32ull << wlog2) * 16) ++wlog2;  // at most 16 float4 per thread
+    const unsigned long long rows_per_cta = kRWarps >> wlog2;
+    const unsigned long long ctas = std::min<unsigned long long>((a.rows + rows_per_cta - 1) / rows_per_cta,
+                                                                 static_cast<unsigned long long>(sm_count()) * 2);
+    row_reread_kernel<MODE><<<static_cast<unsigned>(ctas), kRThreads, 0, stream()>>>(a, wlog2);
+    check_launch("softmax_rows_reread");
+}
+
 template <int MODE, bool BULK>
 static void launch_rows_mode(const RowArgs& a, unsigned C, std::size_t smem) {
     static bool configured = false;
@@ -962,6 +1204,12 @@ static void launch_family(RowArgs a, std::size_t outer, std::size_t length, std:
             ce_rows_kernel<<<static_cast<unsigned>(ctas), kThreads, 0, stream()>>>(a);
             check_launch("cross_entropy_rows");
             return;
+        }
+        if constexpr (MODE != CE_FWD) {
+            if (aligned && length <= kRereadMaxL) {
+                launch_rows_reread<MODE>(a);
+                return;
+            }
         }
         if (aligned) {
             constexpr unsigned NB = PipeTraits<MODE>::NBUF;
