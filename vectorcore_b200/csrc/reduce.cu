@@ -16,12 +16,10 @@
 // SM count), so results do not depend on the launch configuration.
 #include "vc_internal.cuh"
 
-#include <cuda.h>
-#include <cudaTypedefs.h>
-
 #include <algorithm>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 namespace vc {
 
@@ -603,24 +601,27 @@ binary_backward_flat(const float* __restrict__ a, const float* __restrict__ b, c
 // full pass per reduced axis for each (src/autograd.cpp:50-72 after
 // src/ops.cpp:124-156). Canonical layout after dropping unit dims and merging
 // neighbours of one class:
-//   L -- the innermost run, kept by both gradients (float4 lanes);
+//   L -- the innermost run, kept by both gradients (float4 columns);
 //   U -- the dims only a spans (da keeps them, db reduces them), at most two;
 //   V -- the dims only b spans (db keeps them, da reduces them), V <= 128;
 //   K -- outer dims both span (independent problems, grid.z), at most two.
-// A CTA owns 32 floats of L (one 128-byte line of every row), all V and a
-// segment of U. TMA streams, per u, the [V][32] tile of g and the [32] line
-// of a into a ring of kFStages shared-memory stages (tensor maps over g and
-// a; the copy engine keeps the next steps in flight while the CTA computes).
-// The 512 threads form 64 "slots" of 8 float4 lanes; slot s = (vs, us) takes
-// v = vs + VS*i (its b values live in registers) and the u of tile us of each
-// step. Per step every slot
-//   * folds the vjp_a terms of its v's (float, in i order: at most 2) into one
-//     value per lane; the VS slots of a u are then combined in a fixed tree
-//     (float within a thread's share, double across threads) and da is
-//     written, rounded once;
-//   * adds the vjp_b terms into a per-(v, lane) float block that is flushed
-//     every 8 steps into double accumulators in shared memory; at the end the
-//     US groups are combined in order into db (or into this U segment's
+// A CTA owns 32 floats of L (8 float4 columns), all V and a segment of U.
+// Its 512 threads are 64 row slots x 8 columns; row slot rs = (us, vs) with
+// VS v-slots (a power of two, 4..64) and US = 64 / VS u-slots: a step covers
+// US consecutive u, and the thread owns v = vs + VS*i (i < NV <= 2) at its
+// column for every step, so b sits in registers. Loads are plain 128-bit
+// loads of g, UNR = 8 / NV steps per group, so every thread keeps eight in
+// flight (two 512-thread CTAs per SM keep HBM busy on these 128-byte pieces
+// of 2 MB-strided rows); the group's a rows arrive in shared memory by
+// cp.async one group ahead. Per step
+//   * da: the thread folds its NV terms in float (i order), the 4 v-slots of
+//     a warp (one u) fold in float across lanes (xor 8, then 16), and the
+//     VS / 4 warp partials of a u are combined in double, in a fixed tree,
+//     through an XOR-swizzled shared buffer (conflict-free both ways); da is
+//     written rounded once;
+//   * db: the terms add into a per-(v, column) float block that is flushed
+//     every 8 steps into double accumulators in shared memory; at the end
+//     the US u-slots are combined in order into db (or into this U segment's
 //     partial, summed in segment order by reduce_col_finish).
 // Every combine order depends on the shape only. The float blocks (at most 8
 // terms) add a relative error of a few float ulps of the block; the
@@ -628,12 +629,11 @@ binary_backward_flat(const float* __restrict__ a, const float* __restrict__ b, c
 // tolerance.
 // ---------------------------------------------------------------------------
 constexpr unsigned kFThreads = 512;
-constexpr unsigned kFLanes = 8;                 // float4 lanes per slot
-constexpr unsigned kFSlots = kFThreads / kFLanes;
-constexpr unsigned kFChunk = kFLanes * 4;       // floats of L per CTA
+constexpr unsigned kFCols = 8;                  // float4 columns per CTA
+constexpr unsigned kFChunk = kFCols * 4;        // floats of L per CTA
+constexpr unsigned kFRowSlots = kFThreads / kFCols;
+constexpr unsigned kFWarps = kFThreads / 32;
 constexpr unsigned kFMaxV = 128;
-constexpr unsigned kFMaxNV = kFMaxV / kFSlots;
-constexpr unsigned kFStages = 3;
 constexpr unsigned kFFlush = 8;                 // steps per float block of db
 // CTAs to aim for: 8 waves of 148 SMs x 2 resident CTAs (a constant: the
 // split, and so the result, depends on the shape alone).
@@ -642,309 +642,276 @@ constexpr unsigned long long kFMinUSeg = 128;
 constexpr std::size_t kFMaxSmem = 112 * 1024;
 
 struct FusedDesc {
-    int rank_g, rank_a;          // tensor-map ranks
     int nk;
     unsigned U0, U1;
     FastDiv u1fd;
     long long ua0, ua1;          // da (= a layout) strides of the U dims
+    long long gu0, gu1;          // g strides of the U dims
     unsigned long long kdims[2]; // K dims, outer first
-    long long ka[2], kb[2];      // da / db strides of the K dims
+    long long ka[2], kb[2], kg[2];  // da / db / g strides of the K dims
     int nv;
     unsigned vdims[2];           // V dims, outer first
-    long long vb[2];             // db (= b layout) strides of the V dims
+    long long vb[2], vg[2];      // db (= b layout) / g strides of the V dims
     unsigned U, V;
     unsigned long long L;        // innermost run, a multiple of 4
     unsigned useg, S;            // u positions per segment, segments
-    unsigned VS, US, NV;         // slot split: v-slots, u-slots, v's per slot
-    unsigned vs_log2, tp_log2;   // log2 of VS and of the threads per da output
-    unsigned stage_bytes;        // one step: US tiles of g ([V][32]) and of a ([32])
-    unsigned scratch_floats;     // one da-partial buffer: [US * 32 outputs][VS + 1]
+    unsigned VS, US;             // v-slots, u-slots per step
+    unsigned vs_log2;
     unsigned long long db_count; // elements of db (the partial stride)
     double* da_d;                // unrounded outputs (shard partials) when set
     double* db_d;
-    unsigned* err;               // device error word (bounded waits)
 };
 
-// Tiled TMA load (no multicast) of one box into this CTA's shared memory;
-// coordinates innermost first, those beyond `rank` ignored.
-__device__ __forceinline__ void tma_load(void* dst, const CUtensorMap* map, int rank, int c0, int c1, int c2, int c3,
-                                         int c4, unsigned long long* bar) {
-    const unsigned d = smem_addr(dst), b = smem_addr(bar);
-    const unsigned long long m = reinterpret_cast<unsigned long long>(map);
-    if (rank == 3)
-        asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-                     " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(d), "l"(m), "r"(c0), "r"(c1), "r"(c2), "r"(b) : "memory");
-    else if (rank == 4)
-        asm volatile("cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-                     " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(d), "l"(m), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
-                     "r"(b) : "memory");
-    else
-        asm volatile("cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-                     " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(d), "l"(m), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
-                     "r"(c4), "r"(b) : "memory");
-}
-
-__device__ __forceinline__ long long decode_vb(const FusedDesc& d, unsigned v) {
-    long long bo = 0;
+__device__ __forceinline__ long long decode_v(const FusedDesc& d, unsigned v, const long long* st) {
+    long long o = 0;
     for (int i = d.nv - 1; i >= 0; --i) {
         const unsigned c = v % d.vdims[i];
         v /= d.vdims[i];
-        bo += static_cast<long long>(c) * d.vb[i];
+        o += static_cast<long long>(c) * st[i];
     }
-    return bo;
+    return o;
 }
 
 __device__ __forceinline__ float4 add4(float4 x, float4 y) { return make_float4(x.x + y.x, x.y + y.y, x.z + y.z, x.w + y.w); }
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-template <int OP>
+template <unsigned NV> __host__ __device__ constexpr unsigned fused_unroll() { return 8u / NV; }
+
+// Shared memory of one CTA: [2][UNR][kFWarps][32] float da partials,
+// [NV][2][kFThreads] double2 db accumulators, [2][UNR][US][kFCols] float4 a rows.
+template <unsigned NV>
+static std::size_t fused_smem(unsigned US) {
+    constexpr unsigned UNR = fused_unroll<NV>();
+    return 2ull * UNR * kFWarps * 32 * sizeof(float) + NV * 2ull * kFThreads * sizeof(double2) +
+           2ull * UNR * US * kFCols * sizeof(float4);
+}
+
+// The four row slots of a warp (lanes c, c+8, c+16, c+24: the four v-slots
+// of one u at column c) fold their float4 into one float per lane: a
+// reduce-scatter in the fixed tree ((r0 + r1) + (r2 + r3)) per component,
+// three shuffles instead of eight. Lane row slot k ends with component
+// (k & 1) * 2 + (k >> 1) of the column.
+__device__ __forceinline__ float fold4_scatter(float4 v, unsigned k) {
+    const bool odd = k & 1u, high = k & 2u;
+    float keep0 = odd ? v.z : v.x, keep1 = odd ? v.w : v.y;
+    const float send0 = odd ? v.x : v.z, send1 = odd ? v.y : v.w;
+    keep0 += __shfl_xor_sync(0xffffffffu, send0, 8);
+    keep1 += __shfl_xor_sync(0xffffffffu, send1, 8);
+    const float keep = high ? keep1 : keep0, send = high ? keep0 : keep1;
+    return keep + __shfl_xor_sync(0xffffffffu, send, 16);
+}
+
+// FULL: every v of the thread exists (V = NV * VS) and every column is
+// inside L (L a multiple of 32), so the per-row and per-column checks go.
+template <int OP, unsigned NV, bool FULL>
 __global__ void __launch_bounds__(kFThreads, 2)
-bcast_backward_fused(const __grid_constant__ CUtensorMap gmap, const __grid_constant__ CUtensorMap amap,
-                     const float* __restrict__ b, const FusedDesc d, float* __restrict__ da,
-                     float* __restrict__ db, double* __restrict__ partial) {
-    constexpr bool NEED_A = OP == VC_MUL || OP == VC_DIV;
-    constexpr bool NEED_B = OP == VC_MUL || OP == VC_DIV;
-    // dynamic shared memory: [kFStages] steps of ([US][V][32] g, [US][32] a),
-    // [US][V][32] double db accumulators, [2][slots][32] float da partials
-    extern __shared__ __align__(1024) unsigned char fsm[];
-    const unsigned g_tile = d.V * kFChunk;  // floats of one g tile
-    double* dacc = reinterpret_cast<double*>(fsm + kFStages * d.stage_bytes);
-    const unsigned acc_count = d.US * d.V * kFChunk;
-    float* scratch = reinterpret_cast<float*>(dacc + acc_count);  // [2][scratch_floats]
-    __shared__ unsigned long long full[kFStages];
-    __shared__ long long s_uao[2][kFSlots];  // da offset of each u-slot's u, by step parity
+bcast_backward_fused(const float* __restrict__ g, const float* __restrict__ a, const float* __restrict__ b,
+                     const FusedDesc d, float* __restrict__ da, float* __restrict__ db,
+                     double* __restrict__ partial) {
+    constexpr unsigned UNR = fused_unroll<NV>();
+    constexpr bool NEED_AB = OP == VC_MUL || OP == VC_DIV;
+    extern __shared__ __align__(16) unsigned char fsm[];
+    float* part = reinterpret_cast<float*>(fsm);
+    double2* dacc = reinterpret_cast<double2*>(part + 2 * UNR * kFWarps * 32);
+    float4* arow = reinterpret_cast<float4*>(dacc + NV * 2 * kFThreads);
 
-    const unsigned lane = threadIdx.x % kFLanes, slot = threadIdx.x / kFLanes;
-    const unsigned vs = slot & (d.VS - 1), us = slot >> d.vs_log2;
+    const unsigned t = threadIdx.x, c = t & (kFCols - 1), rs = t / kFCols, w = t >> 5, lane = t & 31;
+    const unsigned rk = lane >> 3;  // row slot within the warp
+    const unsigned vs = rs & (d.VS - 1), us = rs >> d.vs_log2;
     const unsigned long long l0 = static_cast<unsigned long long>(blockIdx.x) * kFChunk;
-    const bool lane_ok = l0 + lane * 4 < d.L;
+    const bool col_ok = FULL || l0 + 4 * c < d.L;
     const unsigned seg = blockIdx.y;
     const unsigned u0 = seg * d.useg;
     const unsigned u1 = min(d.U, u0 + d.useg);
     const unsigned nsteps = (u1 - u0 + d.US - 1) / d.US;
+    const unsigned ngroups = (nsteps + UNR - 1) / UNR;
 
-    // K position of this CTA: coordinates (outer first) and da / db offsets
-    int kc[2] = {0, 0};
-    long long ka = 0, kb = 0;
+    // K position of this CTA: da / db / g offsets
+    long long ka = 0, kb = 0, kg = 0;
     {
         unsigned long long r = blockIdx.z;
         for (int i = d.nk - 1; i >= 0; --i) {
-            const unsigned long long c = r % d.kdims[i];
+            const unsigned long long q = r % d.kdims[i];
             r /= d.kdims[i];
-            kc[i] = static_cast<int>(c);
-            ka += static_cast<long long>(c) * d.ka[i];
-            kb += static_cast<long long>(c) * d.kb[i];
+            ka += static_cast<long long>(q) * d.ka[i];
+            kb += static_cast<long long>(q) * d.kb[i];
+            kg += static_cast<long long>(q) * d.kg[i];
         }
     }
-    float4 breg[kFMaxNV];
-    bool vok[kFMaxNV];
+    const float* ak = a + ka + static_cast<long long>(l0);
+
+    float4 breg[NV], facc[NV];
+    const float* gp[NV];  // this thread's rows of g at u = 0
+    bool vok[NV];
 #pragma unroll
-    for (unsigned i = 0; i < kFMaxNV; ++i) {
+    for (unsigned i = 0; i < NV; ++i) {
         const unsigned v = vs + d.VS * i;
-        vok[i] = i < d.NV && v < d.V;
-        breg[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (NEED_B && vok[i] && lane_ok)
-            breg[i] = ldg4(b + kb + decode_vb(d, v) + static_cast<long long>(l0 + lane * 4));
+        vok[i] = FULL || (v < d.V && col_ok);
+        gp[i] = g + kg + (vok[i] ? decode_v(d, v, d.vg) : 0) + static_cast<long long>(l0 + 4 * c);
+        breg[i] = NEED_AB && vok[i] ? ldg4(b + kb + decode_v(d, v, d.vb) + static_cast<long long>(l0 + 4 * c))
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+        facc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        dacc[(i * 2 + 0) * kFThreads + t] = make_double2(0.0, 0.0);
+        dacc[(i * 2 + 1) * kFThreads + t] = make_double2(0.0, 0.0);
     }
-    for (unsigned i = threadIdx.x; i < acc_count; i += kFThreads) dacc[i] = 0.0;
-    if (threadIdx.x == 0) {
-        for (unsigned s = 0; s < kFStages; ++s) mbar_init(&full[s], 1);
-        mbar_fence_init();
-    }
-    __syncthreads();
-
-    // Tensor-map coordinates beyond (L, U1, U0): g has the V dims (always 0)
-    // then the K dims, innermost first; a has the K dims, innermost first.
-    int gk[2] = {0, 0}, ak[2] = {0, 0};
-    if (d.nk >= 1) {
-        ak[0] = kc[d.nk - 1];
-        if (d.nv == 1) gk[1] = kc[d.nk - 1];
-    }
-    if (d.nk == 2) ak[1] = kc[0];
-    // producer (thread 0): step t -> stage t % kFStages, u = u0 + t*US + j
-    unsigned p_c1 = 0, p_c0 = 0;  // U coordinates of the next u to issue
-    unsigned issued = 0;          // steps issued
-    if (threadIdx.x == 0) d.u1fd.divmod(u0, p_c0, p_c1);
-    auto issue = [&](unsigned t) {
-        unsigned char* st = fsm + (t % kFStages) * d.stage_bytes;
-        const unsigned first = u0 + t * d.US;
-        const unsigned n = min(d.US, u1 - first);
-        mbar_expect_tx(&full[t % kFStages],
-                       n * (g_tile + (NEED_A ? kFChunk : 0u)) * static_cast<unsigned>(sizeof(float)));
-        for (unsigned j = 0; j < n; ++j) {
-            const int x = static_cast<int>(l0), c1 = static_cast<int>(p_c1), c0 = static_cast<int>(p_c0);
-            tma_load(reinterpret_cast<float*>(st) + j * g_tile, &gmap, d.rank_g, x, c1, c0, gk[0], gk[1],
-                     &full[t % kFStages]);
-            if (NEED_A)
-                tma_load(reinterpret_cast<float*>(st) + d.US * g_tile + j * kFChunk, &amap, d.rank_a, x, c1, c0,
-                         ak[0], ak[1], &full[t % kFStages]);
-            if (++p_c1 == d.U1) { p_c1 = 0; ++p_c0; }
+    // a rows of group n (UNR steps x US u x kFCols columns) into arow[n & 1]
+    auto fetch_a = [&](unsigned n) {
+        float4* dst = arow + (n & 1u) * UNR * d.US * kFCols;
+        const unsigned count = UNR * d.US * kFCols;
+        for (unsigned e = t; e < count; e += kFThreads) {
+            const unsigned cc = e % kFCols, q = e / kFCols;  // q = k * US + u-slot
+            const unsigned u = u0 + n * UNR * d.US + q;
+            if (u < u1 && (FULL || l0 + 4 * cc < d.L)) {
+                unsigned c0, c1;
+                d.u1fd.divmod(u, c0, c1);
+                cp_async16(dst + e, ak + static_cast<long long>(c0) * d.ua0 + static_cast<long long>(c1) * d.ua1 + 4 * cc);
+            }
         }
-        ++issued;
     };
-    if (threadIdx.x == 0)
-        for (unsigned t = 0; t < kFStages && t < nsteps; ++t) issue(t);
-
-    // da offset of this slot's u (slots with vs == 0 publish it per step)
-    unsigned c_c0, c_c1;
-    d.u1fd.divmod(u0 + us, c_c0, c_c1);
-    long long uao = static_cast<long long>(c_c0) * d.ua0 + static_cast<long long>(c_c1) * d.ua1;
-
-    float4 facc[kFMaxNV];
-#pragma unroll
-    for (unsigned i = 0; i < kFMaxNV; ++i) facc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    const unsigned tp = 1u << d.tp_log2;  // slot lanes per da output in the combine
-    // Only thread 0 polls a stage's mbarrier (512 threads polling one word
-    // would crowd the shared-memory pipe); the CTA barrier that follows
-    // publishes the stage, and the success flag, to every thread.
-    unsigned waited = 0;  // steps thread 0 has seen complete
-    bool ok = true;
-    if (threadIdx.x == 0 && nsteps > 0) {
-        ok = mbar_wait_bounded(&full[0], 0u, d.err);
-        waited = ok ? 1u : 0u;
+    if (NEED_AB) {
+        fetch_a(0);
+        cp_async_wait_all();
     }
-    ok = __syncthreads_and(ok) != 0;
-    unsigned u = u0 + us;
-    for (unsigned t = 0; t < nsteps; ++t, u += d.US) {
-        const unsigned stg = t % kFStages;
-        const float* sg = reinterpret_cast<const float*>(fsm + stg * d.stage_bytes);
-        float4 dap = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (u < u1 && lane_ok) {
-            const float4 av = NEED_A ? reinterpret_cast<const float4*>(sg + d.US * g_tile + us * kFChunk)[lane]
-                                     : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-            for (unsigned i = 0; i < kFMaxNV; ++i) {
-                if (!vok[i]) continue;
-                const float4 gv = reinterpret_cast<const float4*>(sg + us * g_tile + (vs + d.VS * i) * kFChunk)[lane];
-                float4 ga, gb;
-                bb_four<OP>(av, breg[i], gv, ga, gb);
-                dap = i == 0 ? ga : add4(dap, ga);
-                facc[i] = add4(facc[i], gb);
-            }
-        }
-        // da: the VS slots of each u, combined in a fixed tree. Partials go
-        // to [slot][32] rows with the float4 column XOR-swizzled by slot % 8,
-        // so both this store and the combine's reads (4 outputs x 8 slots per
-        // warp instruction) are free of bank conflicts.
-        float* sc = scratch + (t & 1u) * d.scratch_floats;
-        reinterpret_cast<float4*>(sc)[slot * kFLanes + (lane ^ (slot & 7u))] = dap;
-        if (vs == 0 && lane == 0) s_uao[t & 1u][us] = uao;
-        bool next_ok = ok;
-        if (threadIdx.x == 0 && ok && t + 1 < nsteps) {
-            next_ok = mbar_wait_bounded(&full[(t + 1) % kFStages], ((t + 1) / kFStages) & 1u, d.err);
-            if (next_ok) waited = t + 2;
-        }
-        ok = __syncthreads_and(next_ok) != 0;
-        // every thread is done with stage stg: refill it with step t + kFStages
-        if (threadIdx.x == 0 && ok && t + kFStages < nsteps) {
-            fence_proxy_async_smem();
-            issue(t + kFStages);
-        }
-        // A warp pass covers go = 32 / gs outputs x gs slot lanes (gs =
-        // min(VS, 8)); lane (j, k) adds slots j, j + gs, ... of its output in
-        // double, then the gs lanes meet in a double xor tree.
-        for (unsigned o0 = (threadIdx.x >> 5) * (32u >> d.tp_log2); o0 < d.US * kFChunk;
-             o0 += (kFThreads / 32) * (32u >> d.tp_log2)) {
-            const unsigned go = 32u >> d.tp_log2;
-            const unsigned o = o0 + ((threadIdx.x & 31) & (go - 1)), j = (threadIdx.x & 31) >> (5 - d.tp_log2);
-            const unsigned ou = o / kFChunk, ol = o % kFChunk;
-            double s = 0.0;
-            for (unsigned v = j; v < d.VS; v += tp) {
-                const unsigned sl = ou * d.VS + v;
-                s += static_cast<double>(sc[sl * kFChunk + ((((ol >> 2) ^ (sl & 7u)) << 2) | (ol & 3u))]);
-            }
-            for (unsigned m = go; m < 32; m <<= 1) s += __shfl_xor_sync(0xffffffffu, s, m);
-            if (j == 0 && u0 + ou + t * d.US < u1 && l0 + ol < d.L) {
-                const long long off = ka + s_uao[t & 1u][ou] + static_cast<long long>(l0 + ol);
-                if (d.da_d) d.da_d[off] = s;
-                else da[off] = static_cast<float>(s);
-            }
-        }
-        // db: flush the float blocks into the double accumulators
-        if ((t + 1) % kFFlush == 0 || t + 1 == nsteps) {
-#pragma unroll
-            for (unsigned i = 0; i < kFMaxNV; ++i) {
-                if (vok[i] && lane_ok) {
-                    double* p = dacc + (static_cast<unsigned long long>(us) * d.V + vs + d.VS * i) * kFChunk + lane * 4;
-                    p[0] += static_cast<double>(facc[i].x);
-                    p[1] += static_cast<double>(facc[i].y);
-                    p[2] += static_cast<double>(facc[i].z);
-                    p[3] += static_cast<double>(facc[i].w);
-                }
-                facc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-        }
-        // advance this slot's u by US (carry into U0)
-        c_c1 += d.US;
-        uao += static_cast<long long>(d.US) * d.ua1;
-        while (c_c1 >= d.U1) {
-            c_c1 -= d.U1;
-            uao += d.ua0 - static_cast<long long>(d.U1) * d.ua1;
-        }
-    }
-    // a wait that gave up may leave copies in flight: wait for them (bounded)
-    if (!ok && threadIdx.x == 0)
-        for (unsigned t = waited; t < issued; ++t) mbar_wait_bounded(&full[t % kFStages], (t / kFStages) & 1u, d.err);
     __syncthreads();
-    // db: the US groups in order, then this segment's partial (or db itself)
-    for (unsigned o = threadIdx.x; o < d.V * kFChunk; o += kFThreads) {
-        const unsigned v = o / kFChunk, ol = o % kFChunk;
-        if (l0 + ol >= d.L) continue;
-        double s = 0.0;
-        for (unsigned x = 0; x < d.US; ++x) s += dacc[(static_cast<unsigned long long>(x) * d.V + v) * kFChunk + ol];
-        const long long off = kb + decode_vb(d, v) + static_cast<long long>(l0 + ol);
-        if (d.S > 1) partial[static_cast<unsigned long long>(seg) * d.db_count + off] = s;
-        else if (d.db_d) d.db_d[off] = s;
-        else db[off] = static_cast<float>(s);
-    }
-}
 
-// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
-// against libcuda); null when the driver does not provide it.
-static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q{};
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    });
-    return fn;
-}
+    // One group of UNR steps; CHECK: some step of it lies past the segment.
+    auto group = [&](unsigned n, auto check) {
+        constexpr bool CHECK = decltype(check)::value;
+        const unsigned s0 = n * UNR;
+        float4 gv[UNR][NV];
+        bool sok[UNR];
+#pragma unroll
+        for (unsigned k = 0; k < UNR; ++k) {
+            const unsigned u = u0 + (s0 + k) * d.US + us;
+            sok[k] = !CHECK || u < u1;
+            unsigned c0 = 0, c1 = 0;
+            if (sok[k]) d.u1fd.divmod(u, c0, c1);
+            const long long go = static_cast<long long>(c0) * d.gu0 + static_cast<long long>(c1) * d.gu1;
+#pragma unroll
+            for (unsigned i = 0; i < NV; ++i)
+                gv[k][i] = sok[k] && vok[i] ? ld4_stream(gp[i] + go) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        float* pb = part + (n & 1u) * UNR * kFWarps * 32;
+        const float4* ab = arow + (n & 1u) * UNR * d.US * kFCols;
+#pragma unroll
+        for (unsigned k = 0; k < UNR; ++k) {
+            float4 dap = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (sok[k]) {
+                const float4 av = NEED_AB ? ab[(k * d.US + us) * kFCols + c] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (unsigned i = 0; i < NV; ++i) {
+                    if (!vok[i]) continue;
+                    float4 ga, gb;
+                    bb_four<OP>(av, breg[i], gv[k][i], ga, gb);
+                    dap = i == 0 ? ga : add4(dap, ga);
+                    facc[i] = add4(facc[i], gb);
+                }
+            }
+            pb[(k * kFWarps + w) * 32 + c * 4 + (rk & 1u) * 2 + (rk >> 1)] = fold4_scatter(dap, rk);
+            if ((s0 + k + 1) % kFFlush == 0) {
+#pragma unroll
+                for (unsigned i = 0; i < NV; ++i) {
+                    double2& lo = dacc[(i * 2 + 0) * kFThreads + t];
+                    double2& hi = dacc[(i * 2 + 1) * kFThreads + t];
+                    lo.x += static_cast<double>(facc[i].x);
+                    lo.y += static_cast<double>(facc[i].y);
+                    hi.x += static_cast<double>(facc[i].z);
+                    hi.y += static_cast<double>(facc[i].w);
+                    facc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
+        }
+    };
 
-// A float32 tiled tensor map; dims innermost first, strides in elements
-// (entries 1..rank-1 used). false when the driver rejects it.
-static bool encode_tensor_map(CUtensorMap* map, const float* base, int rank, const unsigned long long* dims,
-                              const long long* strides, const unsigned* box) {
-    auto fn = tensor_map_encoder();
-    if (!fn) return false;
-    cuuint64_t gdim[5], gstride[4];
-    cuuint32_t bdim[5], estride[5];
-    for (int i = 0; i < rank; ++i) {
-        gdim[i] = dims[i];
-        bdim[i] = box[i];
-        estride[i] = 1;
-        if (i > 0) {
-            if (strides[i] <= 0) return false;
-            gstride[i - 1] = static_cast<cuuint64_t>(strides[i]) * sizeof(float);
+    const unsigned gw = d.VS >> 2;  // warps per u
+    for (unsigned n = 0; n < ngroups; ++n) {
+        if (NEED_AB && n + 1 < ngroups) fetch_a(n + 1);
+        if (u0 + ((n + 1) * UNR) * d.US <= u1) group(n, std::false_type{});
+        else group(n, std::true_type{});
+        if (NEED_AB) cp_async_wait_all();  // the next group's a rows
+        __syncthreads();
+        // da: one output float per item, the gw warp partials of its u
+        // added in warp order (double)
+        const unsigned s0 = n * UNR;
+        const float* pb = part + (n & 1u) * UNR * kFWarps * 32;
+        for (unsigned item = t; item < UNR * d.US * 32; item += kFThreads) {
+            const unsigned f = item & 31, q = item >> 5;  // q = k * US + u-slot
+            const unsigned k = q / d.US, uslot = q - k * d.US;
+            const unsigned u = u0 + (s0 + k) * d.US + uslot;
+            if (u >= u1 || (!FULL && l0 + f >= d.L)) continue;
+            const float* src = pb + (k * kFWarps + uslot * gw) * 32 + f;
+            double s = 0.0;
+            for (unsigned j = 0; j < gw; ++j) s += static_cast<double>(src[j * 32]);
+            unsigned c0, c1;
+            d.u1fd.divmod(u, c0, c1);
+            const long long off = ka + static_cast<long long>(c0) * d.ua0 + static_cast<long long>(c1) * d.ua1 +
+                                  static_cast<long long>(l0 + f);
+            if (d.da_d) d.da_d[off] = s;
+            else da[off] = static_cast<float>(s);
         }
     }
-    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, static_cast<cuuint32_t>(rank), const_cast<float*>(base), gdim,
-              gstride, bdim, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    // db: the last float block, then the US u-slots in order
+#pragma unroll
+    for (unsigned i = 0; i < NV; ++i) {
+        double2& lo = dacc[(i * 2 + 0) * kFThreads + t];
+        double2& hi = dacc[(i * 2 + 1) * kFThreads + t];
+        lo.x += static_cast<double>(facc[i].x);
+        lo.y += static_cast<double>(facc[i].y);
+        hi.x += static_cast<double>(facc[i].z);
+        hi.y += static_cast<double>(facc[i].w);
+    }
+    __syncthreads();
+    for (unsigned o = t; o < d.V * kFCols * 2; o += kFThreads) {
+        const unsigned h = o & 1u, cc = (o >> 1) & (kFCols - 1), v = o / (2 * kFCols);
+        if (!FULL && l0 + 4 * cc >= d.L) continue;
+        const unsigned vsl = v & (d.VS - 1), i = v >> d.vs_log2;
+        double2 s = make_double2(0.0, 0.0);
+        for (unsigned x = 0; x < d.US; ++x) {
+            const double2 q = dacc[(i * 2 + h) * kFThreads + ((x << d.vs_log2) + vsl) * kFCols + cc];
+            s.x += q.x;
+            s.y += q.y;
+        }
+        const long long off = kb + decode_v(d, v, d.vb) + static_cast<long long>(l0 + 4 * cc + 2 * h);
+        if (d.S > 1) {
+            double* p = partial + static_cast<unsigned long long>(seg) * d.db_count + off;
+            p[0] = s.x;
+            p[1] = s.y;
+        } else if (d.db_d) {
+            d.db_d[off] = s.x;
+            d.db_d[off + 1] = s.y;
+        } else {
+            db[off] = static_cast<float>(s.x);
+            db[off + 1] = static_cast<float>(s.y);
+        }
+    }
 }
 
-template <int OP>
-static void launch_fused(const CUtensorMap& gm, const CUtensorMap& am, const float* b, const FusedDesc& d,
-                         dim3 grid, std::size_t smem, float* da, float* db, double* partial) {
+template <int OP, unsigned NV, bool FULL>
+static void launch_fused(const float* g, const float* a, const float* b, const FusedDesc& d, dim3 grid,
+                         float* da, float* db, double* partial) {
     static bool configured = false;
     if (!configured) {
-        VC_CUDA(cudaFuncSetAttribute(bcast_backward_fused<OP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        VC_CUDA(cudaFuncSetAttribute(bcast_backward_fused<OP, NV, FULL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(kFMaxSmem)));
         configured = true;
     }
-    bcast_backward_fused<OP><<<grid, kFThreads, smem, stream()>>>(gm, am, b, d, da, db, partial);
+    bcast_backward_fused<OP, NV, FULL><<<grid, kFThreads, fused_smem<NV>(d.US), stream()>>>(g, a, b, d, da, db,
+                                                                                            partial);
+}
+
+template <int OP>
+static void launch_fused_nv(unsigned nv, bool full, const float* g, const float* a, const float* b,
+                            const FusedDesc& d, dim3 grid, float* da, float* db, double* partial) {
+    if (nv == 1) {
+        if (full) launch_fused<OP, 1, true>(g, a, b, d, grid, da, db, partial);
+        else launch_fused<OP, 1, false>(g, a, b, d, grid, da, db, partial);
+    } else {
+        if (full) launch_fused<OP, 2, true>(g, a, b, d, grid, da, db, partial);
+        else launch_fused<OP, 2, false>(g, a, b, d, grid, da, db, partial);
+    }
 }
 
 // Classify the output dims of a two-sided broadcast backward and launch
@@ -1006,9 +973,18 @@ static bool try_fused_bcast_backward(int op, const float* a, const Src& sa, cons
     d.U = static_cast<unsigned>(U);
     d.V = static_cast<unsigned>(V);
     d.nv = nv;
-    for (int i = 0; i < nv; ++i) { d.vdims[i] = static_cast<unsigned>(vd[i].size); d.vb[i] = vd[i].st[2]; }
+    for (int i = 0; i < nv; ++i) {
+        d.vdims[i] = static_cast<unsigned>(vd[i].size);
+        d.vb[i] = vd[i].st[2];
+        d.vg[i] = vd[i].st[0];
+    }
     d.nk = nk;
-    for (int i = 0; i < nk; ++i) { d.kdims[i] = kd[i].size; d.ka[i] = kd[i].st[1]; d.kb[i] = kd[i].st[2]; }
+    for (int i = 0; i < nk; ++i) {
+        d.kdims[i] = kd[i].size;
+        d.ka[i] = kd[i].st[1];
+        d.kb[i] = kd[i].st[2];
+        d.kg[i] = kd[i].st[0];
+    }
     // U as (U0 outer, U1 inner); one U dim is (1, U)
     const Dim uinner = ud[nu - 1];
     const Dim uouter = nu == 2 ? ud[0] : Dim{2, 1, {uinner.st[0] * static_cast<long long>(uinner.size),
@@ -1018,43 +994,15 @@ static bool try_fused_bcast_backward(int op, const float* a, const Src& sa, cons
     d.u1fd = FastDiv(d.U1);
     d.ua1 = uinner.st[1];
     d.ua0 = uouter.st[1];
-    // tensor maps, dims innermost first. g: (L, U1, U0, V dims, K dims);
-    // a: (L, U1, U0, K dims). Boxes: 32 floats x 1 x 1 x all of V; 32 floats.
-    if (3 + nv + nk > 5) return false;
-    unsigned long long gdims[5], adims[5];
-    long long gstr[5], astr[5];
-    unsigned gbox[5], abox[5];
-    int rg = 0, ra = 0;
-    gdims[rg] = d.L; gstr[rg] = 1; gbox[rg++] = kFChunk;
-    adims[ra] = d.L; astr[ra] = 1; abox[ra++] = kFChunk;
-    gdims[rg] = uinner.size; gstr[rg] = uinner.st[0]; gbox[rg++] = 1;
-    adims[ra] = uinner.size; astr[ra] = uinner.st[1]; abox[ra++] = 1;
-    gdims[rg] = uouter.size; gstr[rg] = uouter.st[0]; gbox[rg++] = 1;
-    adims[ra] = uouter.size; astr[ra] = uouter.st[1]; abox[ra++] = 1;
-    for (int i = nv - 1; i >= 0; --i) {
-        gdims[rg] = vd[i].size; gstr[rg] = vd[i].st[0]; gbox[rg++] = static_cast<unsigned>(vd[i].size);
-    }
-    for (int i = nk - 1; i >= 0; --i) {
-        gdims[rg] = kd[i].size; gstr[rg] = kd[i].st[0]; gbox[rg++] = 1;
-        adims[ra] = kd[i].size; astr[ra] = kd[i].st[1]; abox[ra++] = 1;
-    }
-    d.rank_g = rg;
-    d.rank_a = ra;
-    CUtensorMap gm{}, am{};
-    if (!encode_tensor_map(&gm, g, rg, gdims, gstr, gbox)) return false;
-    if (!encode_tensor_map(&am, a, ra, adims, astr, abox)) return false;
-    unsigned vs = 1;
-    while (vs * 2 <= V && vs * 2 <= kFSlots) vs *= 2;
+    d.gu1 = uinner.st[0];
+    d.gu0 = uouter.st[0];
+    unsigned vs = 4;
+    while (vs < V && vs < kFRowSlots) vs *= 2;
     d.VS = vs;
-    d.US = kFSlots / vs;
-    d.NV = static_cast<unsigned>((V + vs - 1) / vs);
-    const unsigned tp = std::min(vs, 8u);
+    d.US = kFRowSlots / vs;
+    const unsigned nvper = static_cast<unsigned>((V + vs - 1) / vs);
     d.vs_log2 = 0;
     while ((1u << d.vs_log2) < vs) ++d.vs_log2;
-    d.tp_log2 = 0;
-    while ((1u << d.tp_log2) < tp) ++d.tp_log2;
-    d.stage_bytes = d.US * (d.V + 1) * kFChunk * static_cast<unsigned>(sizeof(float));
-    d.scratch_floats = kFSlots * kFChunk;
     const unsigned long long chunks = (d.L + kFChunk - 1) / kFChunk;
     unsigned long long S = (kFTargetCtas + chunks * K - 1) / (chunks * K);
     S = std::min<unsigned long long>(S, (U + kFMinUSeg - 1) / kFMinUSeg);
@@ -1066,18 +1014,15 @@ static bool try_fused_bcast_backward(int op, const float* a, const Src& sa, cons
     d.db_count = b_numel;
     d.da_d = da_d;
     d.db_d = db_d;
-    d.err = device_error_word();
-    const std::size_t smem = kFStages * static_cast<std::size_t>(d.stage_bytes) +
-                             static_cast<std::size_t>(d.US) * d.V * kFChunk * sizeof(double) +
-                             2 * static_cast<std::size_t>(d.scratch_floats) * sizeof(float);
-    if (smem > kFMaxSmem) return false;
+    if ((nvper == 1 ? fused_smem<1>(d.US) : fused_smem<2>(d.US)) > kFMaxSmem) return false;
     Scratch partial(d.S > 1 ? static_cast<std::size_t>(d.S) * b_numel * sizeof(double) : 8);
     const dim3 grid(static_cast<unsigned>(chunks), d.S, static_cast<unsigned>(K));
+    const bool full = V == static_cast<unsigned long long>(nvper) * vs && d.L % kFChunk == 0;
     switch (op) {
-        case VC_ADD: launch_fused<VC_ADD>(gm, am, b, d, grid, smem, da, db, partial.as<double>()); break;
-        case VC_SUB: launch_fused<VC_SUB>(gm, am, b, d, grid, smem, da, db, partial.as<double>()); break;
-        case VC_MUL: launch_fused<VC_MUL>(gm, am, b, d, grid, smem, da, db, partial.as<double>()); break;
-        default: launch_fused<VC_DIV>(gm, am, b, d, grid, smem, da, db, partial.as<double>()); break;
+        case VC_ADD: launch_fused_nv<VC_ADD>(nvper, full, g, a, b, d, grid, da, db, partial.as<double>()); break;
+        case VC_SUB: launch_fused_nv<VC_SUB>(nvper, full, g, a, b, d, grid, da, db, partial.as<double>()); break;
+        case VC_MUL: launch_fused_nv<VC_MUL>(nvper, full, g, a, b, d, grid, da, db, partial.as<double>()); break;
+        default: launch_fused_nv<VC_DIV>(nvper, full, g, a, b, d, grid, da, db, partial.as<double>()); break;
     }
     check_launch("bcast_backward_fused");
     if (d.S > 1) {
