@@ -127,6 +127,23 @@ vc_status vc_cuda_upload(void* dst, const void* src, size_t bytes);
  * Replaces MetalBackend::download (metal_backend.hpp:25). */
 vc_status vc_cuda_download(void* dst, const void* src, size_t bytes);
 
+/* Asynchronous host <-> device copies (no counterpart in the reference,
+ * whose MetalBackend::upload / download are synchronous). The host buffer
+ * must be page-locked (vc_cuda_host_alloc), else VC_ERR_INVALID. Each copy
+ * runs on a copy stream of its direction, after the work enqueued before
+ * the call, and returns a ticket; work enqueued later does NOT wait for it
+ * until vc_cuda_transfer_wait(ticket) (which enqueues the dependency and
+ * returns at once). vc_cuda_transfer_sync(ticket) blocks the host until the
+ * copy completed: only then may the host buffer be reused (upload) or read
+ * (download). Freeing a device buffer orders its reuse after the transfers
+ * still touching it; writing it with later work before
+ * vc_cuda_transfer_wait is the caller's race. vc_cuda_synchronize waits for
+ * every transfer too. Not allowed during graph capture. */
+vc_status vc_cuda_upload_async(void* dst, const void* src, size_t bytes, uint64_t* ticket);
+vc_status vc_cuda_download_async(void* dst, const void* src, size_t bytes, uint64_t* ticket);
+vc_status vc_cuda_transfer_wait(uint64_t ticket);
+vc_status vc_cuda_transfer_sync(uint64_t ticket);
+
 /* Device -> device copy and fill, enqueued. */
 vc_status vc_cuda_copy(void* dst, const void* src, size_t bytes);
 vc_status vc_cuda_fill(float* out, size_t count, float value);

@@ -14,7 +14,7 @@ from __future__ import annotations
 
 import ctypes
 import re
-from ctypes import POINTER, c_char_p, c_double, c_float, c_int, c_int64, c_size_t, c_void_p
+from ctypes import POINTER, c_char_p, c_double, c_float, c_int, c_int64, c_size_t, c_uint64, c_void_p
 from pathlib import Path
 
 from . import build as _build
@@ -79,6 +79,10 @@ _SIGS = {
     "vc_cuda_host_free": (c_int, [c_void_p]),
     "vc_cuda_upload": (c_int, [c_void_p, c_void_p, c_size_t]),
     "vc_cuda_download": (c_int, [c_void_p, c_void_p, c_size_t]),
+    "vc_cuda_upload_async": (c_int, [c_void_p, c_void_p, c_size_t, POINTER(c_uint64)]),
+    "vc_cuda_download_async": (c_int, [c_void_p, c_void_p, c_size_t, POINTER(c_uint64)]),
+    "vc_cuda_transfer_wait": (c_int, [c_uint64]),
+    "vc_cuda_transfer_sync": (c_int, [c_uint64]),
     "vc_cuda_copy": (c_int, [c_void_p, c_void_p, c_size_t]),
     "vc_cuda_fill": (c_int, [_f, c_size_t, c_float]),
     "vc_cuda_binary": (c_int, [c_int, _f, _szp, _szp, c_int, _f, _szp, _szp, c_int, _f, _szp, c_int]),

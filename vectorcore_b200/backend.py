@@ -64,6 +64,36 @@ def _p(x):
     return None if x is None else ctypes.c_void_p(x.ptr)
 
 
+class PinnedBuffer:
+    """Page-locked host memory (vc_cuda_host_alloc) viewed as a numpy array:
+    the host side of the asynchronous transfers."""
+
+    def __init__(self, elements: int, dtype=np.float32):
+        self.dtype = np.dtype(dtype)
+        self.size = int(elements)
+        ptr = ctypes.c_void_p()
+        _abi.call("vc_cuda_host_alloc", ctypes.c_size_t(max(self.size, 1) * self.dtype.itemsize), ctypes.byref(ptr))
+        self.ptr = ptr.value
+        buf = (ctypes.c_char * (self.size * self.dtype.itemsize)).from_address(self.ptr)
+        self.array = np.frombuffer(buf, dtype=self.dtype, count=self.size)
+
+    @property
+    def nbytes(self) -> int:
+        return self.size * self.dtype.itemsize
+
+    def close(self) -> None:
+        ptr, self.ptr = getattr(self, "ptr", 0), 0
+        if ptr:
+            self.array = None
+            _abi.lib.vc_cuda_host_free(ctypes.c_void_p(ptr))
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # interpreter shutdown
+            pass
+
+
 class CudaGraph:
     """A replayable capture of the library stream's work (vc_cuda_graph_*).
     The pool blocks allocated while capturing stay reserved for the graph
@@ -160,6 +190,35 @@ class CudaBackend:
         _abi.call("vc_cuda_download", out.ctypes.data_as(ctypes.c_void_p), ctypes.c_void_p(source.ptr),
                   ctypes.c_size_t(out.nbytes))
         return out
+
+    # ---- asynchronous transfers (vc_cuda_upload_async & co.) --------------------
+    def upload_async(self, dst: CudaStorage, src: PinnedBuffer, nbytes: int | None = None) -> int:
+        """Copy a pinned host buffer into dst on the upload copy stream; later
+        work waits for it only after transfer_wait(ticket)."""
+        nb = src.nbytes if nbytes is None else int(nbytes)
+        if nb > dst.nbytes or nb > src.nbytes:
+            raise IndexError("upload_async exceeds a buffer")
+        t = ctypes.c_uint64(0)
+        _abi.call("vc_cuda_upload_async", ctypes.c_void_p(dst.ptr), ctypes.c_void_p(src.ptr), ctypes.c_size_t(nb),
+                  ctypes.byref(t))
+        return int(t.value)
+
+    def download_async(self, dst: PinnedBuffer, src: CudaStorage, nbytes: int | None = None) -> int:
+        """Copy src into a pinned host buffer on the download copy stream,
+        after the work enqueued so far; read dst after transfer_sync(ticket)."""
+        nb = src.nbytes if nbytes is None else int(nbytes)
+        if nb > dst.nbytes or nb > src.nbytes:
+            raise IndexError("download_async exceeds a buffer")
+        t = ctypes.c_uint64(0)
+        _abi.call("vc_cuda_download_async", ctypes.c_void_p(dst.ptr), ctypes.c_void_p(src.ptr),
+                  ctypes.c_size_t(nb), ctypes.byref(t))
+        return int(t.value)
+
+    def transfer_wait(self, ticket: int) -> None:
+        _abi.call("vc_cuda_transfer_wait", ctypes.c_uint64(ticket))
+
+    def transfer_sync(self, ticket: int) -> None:
+        _abi.call("vc_cuda_transfer_sync", ctypes.c_uint64(ticket))
 
     # ---- MetalBackend methods ---------------------------------------------------
     def binary(self, a, a_shape, a_strides, b, b_shape, b_strides, out_shape, op) -> CudaStorage:

@@ -317,13 +317,20 @@ class Tensor:
         return self.reshape((self.numel,))
 
     def to(self, device: str) -> "Tensor":
+        """Copy to the other device (src/tensor.cpp:168-187), without the
+        reference's intermediate host vector: cuda -> cpu downloads straight
+        into the new host storage, cpu -> cuda uploads straight from the host
+        values (large pageable copies are staged through page-locked buffers
+        by the library)."""
         target = parse_device(device)
         if target == self.device:
             return self
+        shape = self._impl.shape
         if target == "cpu":
-            out = Tensor(self.numpy(), False, "cpu")
+            out = Tensor._from(HostStorage(_be().download(self._impl.storage, self.numel)), shape)
         else:
-            out = Tensor(self.numpy(), False, "cuda")
+            values = self._impl.storage.values[: self.numel]
+            out = Tensor._from(_be().upload(values if values.size else np.zeros(0, np.float32)), shape)
         source = self.device
         _attach(out, [self], lambda g: [g.to(source)])
         return out
