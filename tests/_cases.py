@@ -87,6 +87,11 @@ BROADCAST_CASES = [
     ((16, 1, 1000), (1, 9, 1000)),
     ((5, 7, 1, 2052), (7, 3, 2052)),
     ((60, 1), (1, 1028)),
+    # operand reuse along a leading dim (one operand constant along it): a
+    # partial run of the reused dim and a partial column chunk; the operand
+    # kept in registers chosen by footprint, the other constant along rows
+    ((3, 1, 40, 516), (1, 33, 1, 516)),
+    ((2, 20, 1, 260), (2, 1, 17, 1)),
 ]
 
 # sum_to_shape layouts (tests/python/test_performance_paths.py:162-176) plus

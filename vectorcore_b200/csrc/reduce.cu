@@ -210,6 +210,82 @@ reduce_col_kernel(const float* __restrict__ g, const float* __restrict__ p, cons
     }
 }
 
+// COLUMN layout with one reduced dim and no kept outer dims (K = 1): the
+// axis-0 sum of a matrix, the gradient of a row bias, a merged run of
+// reduced dims. A thread owns a float4 column and steps row pointers down its
+// segment with D loads per operand in flight; without the general kernel's
+// per-row coordinate carry and offset arrays it needs fewer registers, so
+// more CTAs stay resident. Same order of double additions as
+// reduce_col_kernel: the results are identical.
+template <int F>
+__global__ void __launch_bounds__(kThreads, operands<F>() == 1 ? 5 : 4)
+reduce_col_simple(const float* __restrict__ g, const float* __restrict__ p, const float* __restrict__ q,
+                  const RedDesc d, float* __restrict__ out, double* __restrict__ partial) {
+    constexpr int NOPS = operands<F>();
+    constexpr int D = NOPS == 1 ? 8 : (NOPS == 2 ? 4 : 2);
+    const unsigned long long i0 = (static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+    if (i0 >= d.inner) return;
+    const unsigned s = blockIdx.z;
+    const unsigned long long r0 = s * d.seg;
+    const unsigned long long r1 = min(d.R, r0 + d.seg);
+    const float* ptr[3] = {g, p, q};
+    const float* base[3];
+    long long step[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        step[k] = d.rs[k][0];
+        base[k] = ptr[k] + static_cast<long long>(r0) * step[k] + (d.is[k] ? static_cast<long long>(i0) : 0);
+    }
+    auto fetch = [&](int k, long long row) -> float4 {
+        const float* a = base[k] + row * step[k];
+        if (d.is[k] == 0) {
+            const float v = __ldg(a);
+            return make_float4(v, v, v, v);
+        }
+        return ldg4(a);
+    };
+    double acc0 = 0.0, acc1 = 0.0, acc2 = 0.0, acc3 = 0.0;
+    auto accumulate = [&](float4 gv, float4 pv, float4 qv) {
+        acc0 += static_cast<double>(vjp<F>(gv.x, pv.x, qv.x));
+        acc1 += static_cast<double>(vjp<F>(gv.y, pv.y, qv.y));
+        acc2 += static_cast<double>(vjp<F>(gv.z, pv.z, qv.z));
+        acc3 += static_cast<double>(vjp<F>(gv.w, pv.w, qv.w));
+    };
+    const long long n = static_cast<long long>(r1 - r0);
+    long long r = 0;
+    for (; r + D <= n; r += D) {
+        float4 v[NOPS][D];
+#pragma unroll
+        for (int j = 0; j < D; ++j)
+#pragma unroll
+            for (int k = 0; k < NOPS; ++k) v[k][j] = fetch(k, r + j);
+#pragma unroll
+        for (int j = 0; j < D; ++j)
+            accumulate(v[0][j], NOPS > 1 ? v[NOPS > 1 ? 1 : 0][j] : v[0][j], NOPS > 2 ? v[NOPS > 2 ? 2 : 0][j] : v[0][j]);
+    }
+    for (; r < n; ++r) {
+        const float4 gv = fetch(0, r);
+        const float4 pv = NOPS > 1 ? fetch(1, r) : gv;
+        const float4 qv = NOPS > 2 ? fetch(2, r) : gv;
+        accumulate(gv, pv, qv);
+    }
+    if (d.S == 1 && d.out_d) {
+        d.out_d[i0] = acc0;
+        d.out_d[i0 + 1] = acc1;
+        d.out_d[i0 + 2] = acc2;
+        d.out_d[i0 + 3] = acc3;
+    } else if (d.S == 1) {
+        st4(out + i0, make_float4(round_out(acc0, d.divisor), round_out(acc1, d.divisor), round_out(acc2, d.divisor),
+                                  round_out(acc3, d.divisor)));
+    } else {
+        double* dst = partial + static_cast<unsigned long long>(s) * d.inner + i0;
+        dst[0] = acc0;
+        dst[1] = acc1;
+        dst[2] = acc2;
+        dst[3] = acc3;
+    }
+}
+
 // Combine COLUMN partials [S][K*inner] in segment order.
 __global__ void __launch_bounds__(kThreads)
 reduce_col_finish(const double* __restrict__ partial, unsigned S, unsigned long long count,
@@ -461,7 +537,9 @@ static void launch_vjp_reduce(const Src ops[3], const size_t* src_shape, int src
                   static_cast<unsigned>(std::min<unsigned long long>(d.K, 65535)), d.S);
         if (grid.x > 0x7fffffffu) fail(VC_ERR_OVERFLOW, "reduction inner run too long");
         Scratch partial(d.S > 1 ? static_cast<std::size_t>(d.S) * d.K * d.inner * sizeof(double) : 8);
-        if (vec) reduce_col_kernel<F, true><<<grid, kThreads, 0, stream()>>>(ops[0].ptr, ops[1].ptr, ops[2].ptr, d, out, partial.as<double>());
+        if (vec && d.nk == 0 && d.nr == 1)
+            reduce_col_simple<F><<<grid, kThreads, 0, stream()>>>(ops[0].ptr, ops[1].ptr, ops[2].ptr, d, out, partial.as<double>());
+        else if (vec) reduce_col_kernel<F, true><<<grid, kThreads, 0, stream()>>>(ops[0].ptr, ops[1].ptr, ops[2].ptr, d, out, partial.as<double>());
         else reduce_col_kernel<F, false><<<grid, kThreads, 0, stream()>>>(ops[0].ptr, ops[1].ptr, ops[2].ptr, d, out, partial.as<double>());
         check_launch("reduce_col");
         if (d.S > 1) {
