@@ -205,6 +205,31 @@ def test_binary_backward_scalar_upstream(backend, port):
     assert_sum_close(host(backend, gb, b.shape), rb, 32, 1.0)
 
 
+# A 0-d upstream makes each gradient constant along the dims only the other
+# operand spans: the reduction runs on the compact shape and is replicated --
+# by the reduction itself when the copies are few and lead the kept dims
+# (single-launch sliced sums, sliced finishes), by a broadcast when they are
+# many, and by a broadcast from a scratch block when they interleave.
+@pytest.mark.parametrize("a_shape,b_shape", [((2, 1, 300, 40), (1, 7, 1, 40)), ((64, 1, 512, 64), (1, 16, 1, 64)),
+                                             ((4, 6), (4, 1)), ((3, 1, 5), (1, 4, 1)), ((1, 9, 1, 33), (6, 1, 70, 33)),
+                                             ((5, 2000), (2000,))])
+def test_binary_backward_scalar_upstream_layouts(backend, port, a_shape, b_shape):
+    rng = np.random.default_rng(int(np.prod(a_shape)) % 1009)
+    a = rng.uniform(0.5, 2, size=a_shape).astype(np.float32)
+    b = rng.uniform(0.5, 2, size=b_shape).astype(np.float32)
+    out_shape = np.broadcast_shapes(a_shape, b_shape)
+    u = np.float32(-0.37)
+    du = dev(backend, np.full((), u, np.float32))
+    da_, db_ = dev(backend, a), dev(backend, b)
+    for name, op in OPS.items():
+        for _ in range(2):  # the replicas of a reused output block are rewritten, not accumulated
+            ga, gb = backend.binary_backward(op, da_, a_shape, db_, b_shape, du, ())
+        ra, rb = port.binary_backward(op, a, b, np.full(out_shape, u, np.float32))
+        for got_s, ref, shape in ((ga, ra, a_shape), (gb, rb, b_shape)):
+            n = int(np.prod(out_shape)) // int(np.prod(shape))
+            assert_sum_close(host(backend, got_s, shape), ref, n, 1.0, what=f"{name} grad {shape} of {out_shape}")
+
+
 @pytest.mark.parametrize("big,small", C.SUM_TO_SHAPE_CASES)
 def test_sum_to_shape(backend, port, big, small):
     g = np.random.default_rng(6).normal(size=big).astype(np.float32)

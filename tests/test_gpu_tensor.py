@@ -380,10 +380,12 @@ def test_fused_bias_relu_sum_matches_reference_golden(golden):
     assert_bitexact(b.grad.numpy(), golden["cfg1_full/db"], "db")
 
 
-@pytest.mark.parametrize("shape", [(1, 1), (3, 5), (65, 130), (200, 4100), (1000, 8)])
+@pytest.mark.parametrize("shape", [(1, 1), (3, 5), (65, 130), (200, 4100), (1000, 8), (1000, 16), (37, 160),
+                                   (4096, 32), (4097, 64), (129, 16400)])
 def test_fused_bias_relu_sum_matches_composed_ops(shape):
     """Odd column counts (scalar path), rows across several 64-row segments,
-    columns across several 1024-column blocks, and a non-unit upstream."""
+    columns across several 1024-column blocks, column strips of 16 floats
+    (up to 4096 rows, then the segmented kernel) and a non-unit upstream."""
     rng = np.random.default_rng(shape[0] * 7 + shape[1])
     x_np = rng.uniform(-1, 1, shape).astype(np.float32)
     b_np = rng.normal(size=shape[1]).astype(np.float32)

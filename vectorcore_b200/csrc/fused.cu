@@ -34,6 +34,18 @@ constexpr unsigned kBwdGroups = kThreads / kBwdLanes;
 constexpr unsigned kBwdRowsPerThread = 4;
 constexpr unsigned kBwdSegRows = kBwdGroups * kBwdRowsPerThread;
 constexpr unsigned kBwdColBlock = kBwdLanes * 4;
+// forward, flat: 512 threads x 8 float4 groups in flight = 4096 groups per CTA
+constexpr unsigned kFwdThreads = 512;
+constexpr unsigned kFwdGroups = 8;
+constexpr unsigned long long kFwdPerCta = kFwdThreads * kFwdGroups;
+// backward, column strips: a CTA owns 16 floats of every row (four float4
+// lanes x 128 row slots, eight rows in flight per thread)
+constexpr unsigned kStripThreads = 512;
+constexpr unsigned kStripLanes = 4;
+constexpr unsigned kStripSlots = kStripThreads / kStripLanes;
+constexpr unsigned kStripRowsInFlight = 8;
+constexpr unsigned kStripCols = kStripLanes * 4;
+constexpr unsigned long long kStripMaxRows = 4096;
 
 __device__ __forceinline__ float relu_of(float h) { return h > 0.0f ? h : 0.0f; }
 
@@ -47,6 +59,62 @@ __device__ __forceinline__ bool arrive_last(unsigned* ticket, unsigned expected,
     __syncthreads();
     if (*s_last) __threadfence();
     return *s_last;
+}
+
+// Forward over x viewed as float4 groups (x rows a multiple of 4 floats,
+// 16-byte aligned). CTA k owns groups [4096 k, 4096 (k + 1)); thread t loads
+// groups t + 512 j (j < 8) together, so the whole tensor is requested in one
+// wave, and adds them in j order. The last CTA to arrive adds the per-CTA
+// partials in CTA order, each thread loading its partials before adding
+// (independent loads, one L2 round trip), then a fixed block tree.
+__global__ void __launch_bounds__(kFwdThreads)
+bias_relu_sum_fwd_wide(const float* __restrict__ x, const float* __restrict__ b, unsigned long long units,
+                       FastDiv cols_fd, double* __restrict__ partial, unsigned* __restrict__ ticket,
+                       float* __restrict__ loss, double* __restrict__ loss_d) {
+    __shared__ double s_red[32];
+    __shared__ bool s_last;
+    pdl_wait();
+    pdl_trigger();
+    const unsigned long long base = static_cast<unsigned long long>(blockIdx.x) * kFwdPerCta;
+    float4 xv[kFwdGroups], bv[kFwdGroups];
+#pragma unroll
+    for (unsigned k = 0; k < kFwdGroups; ++k) {
+        const unsigned long long e = base + k * kFwdThreads + threadIdx.x;
+        if (e < units) {
+            unsigned q, r;
+            cols_fd.divmod(static_cast<unsigned>(e), q, r);
+            xv[k] = ldg4(x + 4 * e);
+            bv[k] = ldg4(b + 4ull * r);
+        }
+    }
+    double acc = 0.0;
+#pragma unroll
+    for (unsigned k = 0; k < kFwdGroups; ++k) {
+        if (base + k * kFwdThreads + threadIdx.x >= units) continue;
+        const float y0 = relu_of(xv[k].x + bv[k].x), y1 = relu_of(xv[k].y + bv[k].y);
+        const float y2 = relu_of(xv[k].z + bv[k].z), y3 = relu_of(xv[k].w + bv[k].w);
+        acc += static_cast<double>((y0 + y1) + (y2 + y3));
+    }
+    acc = block_sum(acc, s_red);
+    if (threadIdx.x == 0) partial[blockIdx.x] = acc;
+    if (!arrive_last(ticket, gridDim.x, &s_last)) return;
+    double t = 0.0;
+    for (unsigned s0 = 0; s0 < gridDim.x; s0 += 4 * kFwdThreads) {
+        double p[4];
+#pragma unroll
+        for (unsigned j = 0; j < 4; ++j) {
+            const unsigned s = s0 + j * kFwdThreads + threadIdx.x;
+            p[j] = s < gridDim.x ? __ldcg(partial + s) : 0.0;
+        }
+#pragma unroll
+        for (unsigned j = 0; j < 4; ++j) t += p[j];
+    }
+    t = block_sum(t, s_red);
+    if (threadIdx.x == 0) {
+        if (loss) *loss = static_cast<float>(t);
+        if (loss_d) *loss_d = t;
+        *ticket = 0;  // ready for the next launch (stream order)
+    }
 }
 
 // Forward over x viewed flat: CTA k owns the 1024 float4 groups (or
@@ -197,6 +265,73 @@ bias_relu_sum_bwd(const float* __restrict__ x, const float* __restrict__ b, cons
     if (threadIdx.x == 0) *ticket = 0;
 }
 
+// Backward for up to 4096 rows whose length is a multiple of 16 floats:
+// CTA k owns columns [16 k, 16 k + 16) of every row, so db needs no
+// cross-CTA step (no counter buffer, atomics or ticket). Thread (slot, lane)
+// = (tid / 4, tid % 4) owns the float4 column 16 k + 4 lane over rows
+// slot + 128 i: it loads eight rows together, writes dx and counts the rows
+// with h > 0. A warp's eight slots meet by shuffles (lanes of one column are
+// 4 apart), the 16 warps through shared memory; integer counts are exact in
+// any order.
+__global__ void __launch_bounds__(kStripThreads)
+bias_relu_sum_bwd_strip(const float* __restrict__ x, const float* __restrict__ b, const float* __restrict__ upstream,
+                        unsigned rows, unsigned long long cols, float* __restrict__ dx, float* __restrict__ db,
+                        double* __restrict__ db_d) {
+    __shared__ unsigned s_cnt[kStripThreads / 32][kStripCols];
+    pdl_wait();
+    pdl_trigger();
+    const float g = __ldg(upstream) + 0.0f;  // broadcast_to(u): u + 0
+    const unsigned lane = threadIdx.x % kStripLanes, slot = threadIdx.x / kStripLanes;
+    const unsigned long long c = static_cast<unsigned long long>(blockIdx.x) * kStripCols + 4ull * lane;
+    const float4 bv = ldg4(b + c);
+    unsigned n0 = 0, n1 = 0, n2 = 0, n3 = 0;
+    for (unsigned r0 = slot; r0 < rows; r0 += kStripSlots * kStripRowsInFlight) {
+        float4 xs[kStripRowsInFlight];
+#pragma unroll
+        for (unsigned k = 0; k < kStripRowsInFlight; ++k) {
+            const unsigned r = r0 + k * kStripSlots;
+            if (r < rows) xs[k] = ldg4(x + r * cols + c);
+        }
+#pragma unroll
+        for (unsigned k = 0; k < kStripRowsInFlight; ++k) {
+            const unsigned r = r0 + k * kStripSlots;
+            if (r >= rows) break;
+            const bool p0 = (xs[k].x + bv.x) > 0.0f, p1 = (xs[k].y + bv.y) > 0.0f;
+            const bool p2 = (xs[k].z + bv.z) > 0.0f, p3 = (xs[k].w + bv.w) > 0.0f;
+            st4_stream(dx + r * cols + c, make_float4(g * (p0 ? 1.0f : 0.0f), g * (p1 ? 1.0f : 0.0f),
+                                                      g * (p2 ? 1.0f : 0.0f), g * (p3 ? 1.0f : 0.0f)));
+            n0 += p0;
+            n1 += p1;
+            n2 += p2;
+            n3 += p3;
+        }
+    }
+#pragma unroll
+    for (unsigned off = kStripLanes; off < 32; off <<= 1) {
+        n0 += __shfl_xor_sync(0xffffffffu, n0, off);
+        n1 += __shfl_xor_sync(0xffffffffu, n1, off);
+        n2 += __shfl_xor_sync(0xffffffffu, n2, off);
+        n3 += __shfl_xor_sync(0xffffffffu, n3, off);
+    }
+    const unsigned warp = threadIdx.x / 32;
+    if (threadIdx.x % 32 < kStripLanes) {
+        s_cnt[warp][4 * lane + 0] = n0;
+        s_cnt[warp][4 * lane + 1] = n1;
+        s_cnt[warp][4 * lane + 2] = n2;
+        s_cnt[warp][4 * lane + 3] = n3;
+    }
+    __syncthreads();
+    if (threadIdx.x < kStripCols) {
+        unsigned t = 0;
+#pragma unroll
+        for (unsigned w = 0; w < kStripThreads / 32; ++w) t += s_cnt[w][threadIdx.x];
+        const unsigned long long col = static_cast<unsigned long long>(blockIdx.x) * kStripCols + threadIdx.x;
+        const double v = db_from_count(g, t, rows);
+        if (db_d) db_d[col] = v;
+        else db[col] = static_cast<float>(v);
+    }
+}
+
 }  // namespace
 
 }  // namespace vc
@@ -225,8 +360,17 @@ vc_status vc_cuda_bias_relu_sum(const float* x, const float* b, size_t rows, siz
     if (ctas > 0x7fffffffull) fail(VC_ERR_OVERFLOW, "bias_relu_sum: tensor too large");
     const bool cols_small = units < (1ull << 32) && cols_units < (1ull << 32);
     const FastDiv cols_fd(cols_small ? static_cast<unsigned>(cols_units) : 1u);
-    Scratch partial(ctas * sizeof(double));
     unsigned* ticket = counters() + kTicketForward;
+    if (vec && cols_small) {
+        const unsigned long long wide = (units + kFwdPerCta - 1) / kFwdPerCta;
+        Scratch partial(wide * sizeof(double));
+        // programmatic launch: this kernel's set-up overlaps the previous kernel's tail
+        launch_pdl(bias_relu_sum_fwd_wide, dim3(static_cast<unsigned>(wide)), dim3(kFwdThreads), 0, stream(), x, b,
+                   units, cols_fd, partial.as<double>(), ticket, loss, loss_partial);
+        check_launch("bias_relu_sum");
+        return VC_OK;
+    }
+    Scratch partial(ctas * sizeof(double));
     if (vec) bias_relu_sum_fwd<true><<<static_cast<unsigned>(ctas), kThreads, 0, stream()>>>(x, b, units, cols_units, cols_fd, cols_small, partial.as<double>(), ticket, loss, loss_partial);
     else bias_relu_sum_fwd<false><<<static_cast<unsigned>(ctas), kThreads, 0, stream()>>>(x, b, units, cols_units, cols_fd, cols_small, partial.as<double>(), ticket, loss, loss_partial);
     check_launch("bias_relu_sum");
@@ -252,11 +396,17 @@ vc_status vc_cuda_bias_relu_sum_backward(const float* x, const float* b, const f
     if (col_blocks > 0x7fffffffull || segs > 65535 || col_blocks * segs > 0xffffffffull)
         fail(VC_ERR_OVERFLOW, "bias_relu_sum_backward: tensor too large");
     if (rows >= (1ull << 32)) fail(VC_ERR_OVERFLOW, "bias_relu_sum_backward: too many rows for 32-bit counts");
+    const bool vec = cols % 4 == 0 && aligned16(x) && aligned16(b) && aligned16(dx);
+    if (vec && cols % kStripCols == 0 && rows <= kStripMaxRows && cols / kStripCols <= 0x7fffffffull) {
+        launch_pdl(bias_relu_sum_bwd_strip, dim3(static_cast<unsigned>(cols / kStripCols)), dim3(kStripThreads), 0,
+                   stream(), x, b, upstream, static_cast<unsigned>(rows), cols, dx, db, db_partial);
+        check_launch("bias_relu_sum_backward");
+        return VC_OK;
+    }
     Scratch counts(cols * sizeof(unsigned));
     VC_CUDA(cudaMemsetAsync(counts.as<unsigned>(), 0, cols * sizeof(unsigned), stream()));
     const dim3 grid(static_cast<unsigned>(col_blocks), static_cast<unsigned>(segs));
     unsigned* ticket = counters() + kTicketBackward;
-    const bool vec = cols % 4 == 0 && aligned16(x) && aligned16(b) && aligned16(dx);
     if (vec) bias_relu_sum_bwd<true><<<grid, kThreads, 0, stream()>>>(x, b, upstream, rows, cols, dx, db, db_partial, counts.as<unsigned>(), ticket);
     else bias_relu_sum_bwd<false><<<grid, kThreads, 0, stream()>>>(x, b, upstream, rows, cols, dx, db, db_partial, counts.as<unsigned>(), ticket);
     check_launch("bias_relu_sum_backward");

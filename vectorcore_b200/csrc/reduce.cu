@@ -30,6 +30,15 @@ constexpr unsigned kThreads = 256;
 // segments (a constant, so the split depends on the problem size alone).
 constexpr unsigned long long kTargetThreads = 1ull << 19;
 constexpr unsigned long long kMinSegment = 16;         // reduced positions per segment (column)
+// Column sums take at most this many segments, so the partials stay small
+// next to the input when the outputs are few (the compact reductions of a
+// broadcast gradient: 1024 columns of 32768 rows).
+constexpr unsigned long long kMaxSumSegments = 512;
+constexpr unsigned kSliceThreads = 1024;               // sliced kernels: 32 outputs x 32 slices
+constexpr unsigned kSlices = kSliceThreads / 32;
+constexpr unsigned long long kSlicedMaxRows = 1024;    // single-launch column sums up to this many rows
+constexpr unsigned long long kSlicedMaxOutputs = 32768;
+constexpr unsigned long long kReplicateMax = 1ull << 20;  // replicas written by the reduction itself, floats
 constexpr unsigned long long kRowTargetCtas = 4096;    // aim for this many (row, segment) CTAs
 constexpr unsigned long long kRowMinSegment = 4096;    // elements per row segment, at least
 
@@ -216,13 +225,16 @@ reduce_col_kernel(const float* __restrict__ g, const float* __restrict__ p, cons
 // segment with D loads per operand in flight; without the general kernel's
 // per-row coordinate carry and offset arrays it needs fewer registers, so
 // more CTAs stay resident. Same order of double additions as
-// reduce_col_kernel: the results are identical.
-template <int F>
+// reduce_col_kernel: the results are identical. G_CONST: operand 0 is one
+// value for the whole reduction (the 0-d upstream gradient of a sum); it is
+// loaded once, and the loads in flight go to the other operands.
+template <int F, bool G_CONST = false>
 __global__ void __launch_bounds__(kThreads, operands<F>() == 1 ? 5 : 4)
 reduce_col_simple(const float* __restrict__ g, const float* __restrict__ p, const float* __restrict__ q,
                   const RedDesc d, float* __restrict__ out, double* __restrict__ partial) {
     constexpr int NOPS = operands<F>();
-    constexpr int D = NOPS == 1 ? 8 : (NOPS == 2 ? 4 : 2);
+    constexpr int LOADED = NOPS - (G_CONST ? 1 : 0);
+    constexpr int D = LOADED <= 1 ? 8 : (LOADED == 2 ? 4 : 2);
     const unsigned long long i0 = (static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
     if (i0 >= d.inner) return;
     const unsigned s = blockIdx.z;
@@ -236,7 +248,9 @@ reduce_col_simple(const float* __restrict__ g, const float* __restrict__ p, cons
         step[k] = d.rs[k][0];
         base[k] = ptr[k] + static_cast<long long>(r0) * step[k] + (d.is[k] ? static_cast<long long>(i0) : 0);
     }
+    const float gc = G_CONST ? __ldg(g) : 0.0f;
     auto fetch = [&](int k, long long row) -> float4 {
+        if (G_CONST && k == 0) return make_float4(gc, gc, gc, gc);
         const float* a = base[k] + row * step[k];
         if (d.is[k] == 0) {
             const float v = __ldg(a);
@@ -307,6 +321,156 @@ reduce_col_finish(const double* __restrict__ partial, unsigned S, unsigned long 
         if (out_d) out_d[o] = acc;
         else out[o] = round_out(acc, divisor);
     }
+}
+
+// Write the 32 results of a sliced CTA (s_res) to `rep` consecutive copies
+// of the output block: the compact result of a broadcast gradient, replicated
+// along the leading dims every operand is constant on.
+__device__ __forceinline__ void write_replicas(const float* s_res, float* __restrict__ out, unsigned long long count,
+                                               unsigned long long rep) {
+    const unsigned lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const unsigned long long o = static_cast<unsigned long long>(blockIdx.x) * 32 + lane;
+    if (o >= count) return;
+    const float v = s_res[lane];
+    for (unsigned long long k = w; k < rep; k += kSlices) out[k * count + o] = v;
+}
+
+// Combine COLUMN partials [S][count] when the outputs are few and the
+// segments many (a plain thread per output would walk thousands of partials
+// one L2 round trip per eight). A CTA owns 32 outputs; warp w adds the
+// partials of segments [w * per, (w + 1) * per) in segment order, eight in
+// flight, and the 32 slice sums of an output are added in slice order. The
+// order depends on S alone. Float results go to `rep` copies (write_replicas).
+__global__ void __launch_bounds__(kSliceThreads)
+reduce_col_finish_sliced(const double* __restrict__ partial, unsigned S, unsigned long long count,
+                         float divisor, float* __restrict__ out, double* __restrict__ out_d,
+                         unsigned long long rep) {
+    __shared__ double s_slice[kSlices][32];
+    __shared__ float s_res[32];
+    const unsigned lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const unsigned long long o = static_cast<unsigned long long>(blockIdx.x) * 32 + lane;
+    const unsigned per = (S + kSlices - 1) / kSlices;
+    const unsigned s0 = min(S, w * per), s1 = min(S, s0 + per);
+    double acc = 0.0;
+    if (o < count) {
+        unsigned s = s0;
+        for (; s + 8 <= s1; s += 8) {
+            double v[8];
+#pragma unroll
+            for (unsigned k = 0; k < 8; ++k) v[k] = __ldg(partial + static_cast<unsigned long long>(s + k) * count + o);
+#pragma unroll
+            for (unsigned k = 0; k < 8; ++k) acc += v[k];
+        }
+        for (; s < s1; ++s) acc += __ldg(partial + static_cast<unsigned long long>(s) * count + o);
+    }
+    s_slice[w][lane] = acc;
+    __syncthreads();
+    if (w == 0) {
+        double t = 0.0;
+#pragma unroll
+        for (unsigned j = 0; j < kSlices; ++j) t += s_slice[j][lane];
+        if (out_d) {
+            if (o < count) out_d[o] = t;
+        } else {
+            s_res[lane] = round_out(t, divisor);
+        }
+    }
+    if (out_d) return;
+    __syncthreads();
+    write_replicas(s_res, out, count, rep);
+}
+
+// out[k * n + j] = out[j] for k in [1, rep): copies of the block just
+// written at the front of the same buffer (the compact result of a broadcast
+// gradient), as a store stream. Thread t of the grid owns float4 groups
+// t, t + T, ... of the copies, four in flight; the source group comes from
+// L1/L2 (the block is small and every copy reads it). n % 4 == 0 and `out`
+// 16-byte aligned; (rep - 1) * n / 4 < 2^32 (FastDiv).
+__global__ void __launch_bounds__(kThreads)
+replicate_front_block(float* __restrict__ out, unsigned long long n4, FastDiv n4_fd, unsigned long long total4) {
+    const float4* src = reinterpret_cast<const float4*>(out);
+    float4* dst = reinterpret_cast<float4*>(out) + n4;
+    const unsigned long long T = static_cast<unsigned long long>(gridDim.x) * blockDim.x;
+    unsigned long long i = static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    for (; i + 3 * T < total4; i += 4 * T) {
+        float4 v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            unsigned q, r;
+            n4_fd.divmod(static_cast<unsigned>(i + k * T), q, r);
+            v[k] = __ldg(src + r);
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) __stcs(dst + i + k * T, v[k]);
+    }
+    for (; i < total4; i += T) {
+        unsigned q, r;
+        n4_fd.divmod(static_cast<unsigned>(i), q, r);
+        __stcs(dst + i, __ldg(src + r));
+    }
+}
+
+// Column sums over a single reduced dim of at most kSlicedMaxRows rows and// Column sums over a single reduced dim of at most kSlicedMaxRows rows and
+// few outputs, in ONE launch (no partials, no finish): a CTA owns 32
+// consecutive outputs, one per lane; warp w adds rows [w * per, (w + 1) * per)
+// of its lane's column in row order, eight rows in flight, and the 32 slice
+// sums of an output are added in slice order (an order fixed by R alone).
+// Float results go to `rep` copies (write_replicas).
+template <int F>
+__global__ void __launch_bounds__(kSliceThreads)
+reduce_col_sliced(const float* __restrict__ g, const float* __restrict__ p, const float* __restrict__ q,
+                  const RedDesc d, float* __restrict__ out, unsigned long long rep) {
+    constexpr int NOPS = operands<F>();
+    __shared__ double s_slice[kSlices][32];
+    __shared__ float s_res[32];
+    const unsigned lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const unsigned long long l = static_cast<unsigned long long>(blockIdx.x) * 32 + lane;
+    const unsigned long long per = (d.R + kSlices - 1) / kSlices;
+    const unsigned long long r0 = min(d.R, w * per), r1 = min(d.R, r0 + per);
+    double acc = 0.0;
+    if (l < d.inner) {
+        const float* ptr[3] = {g, p, q};
+        const float* base[3];
+        long long step[3];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            step[k] = d.rs[k][0];
+            base[k] = ptr[k] + static_cast<long long>(r0) * step[k] + static_cast<long long>(l) * d.is[k];
+        }
+        const long long n = static_cast<long long>(r1 - r0);
+        long long r = 0;
+        for (; r + 8 <= n; r += 8) {
+            float v[3][8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+#pragma unroll
+                for (int k = 0; k < NOPS; ++k) v[k][j] = __ldg(base[k] + (r + j) * step[k]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                acc += static_cast<double>(vjp<F>(v[0][j], NOPS > 1 ? v[1][j] : 0.0f, NOPS > 2 ? v[2][j] : 0.0f));
+        }
+        for (; r < n; ++r) {
+            const float gv = __ldg(base[0] + r * step[0]);
+            const float pv = NOPS > 1 ? __ldg(base[1] + r * step[1]) : 0.0f;
+            const float qv = NOPS > 2 ? __ldg(base[2] + r * step[2]) : 0.0f;
+            acc += static_cast<double>(vjp<F>(gv, pv, qv));
+        }
+    }
+    s_slice[w][lane] = acc;
+    __syncthreads();
+    if (w == 0) {
+        double t = 0.0;
+#pragma unroll
+        for (unsigned j = 0; j < kSlices; ++j) t += s_slice[j][lane];
+        if (d.out_d) {
+            if (l < d.inner) d.out_d[l] = t;
+        } else {
+            s_res[lane] = round_out(t, d.divisor);
+        }
+    }
+    if (d.out_d) return;
+    __syncthreads();
+    write_replicas(s_res, out, d.inner, rep);
 }
 
 // ---------------------------------------------------------------------------
@@ -433,9 +597,12 @@ static Src align(const float* ptr, const size_t* shape, int rank, const size_t* 
     return s;
 }
 
+// Returns whether the float output was written `rep` times (consecutive
+// copies of the target block); otherwise only the first copy is written.
 template <int F>
-static void launch_vjp_reduce(const Src ops[3], const size_t* src_shape, int src_rank, const size_t* t_shape,
-                              int t_rank, float* out, float divisor, double* out_d = nullptr) {
+static bool launch_vjp_reduce(const Src ops[3], const size_t* src_shape, int src_rank, const size_t* t_shape,
+                              int t_rank, float* out, float divisor, double* out_d = nullptr,
+                              unsigned long long rep = 1) {
     // 1. classify source dims: 0 drop (size 1), 1 kept, 2 reduced.
     if (t_rank > src_rank) fail(VC_ERR_INVALID, "sum_to_shape: cannot reduce to a larger rank");
     const int lead = src_rank - t_rank;
@@ -467,10 +634,38 @@ static void launch_vjp_reduce(const Src ops[3], const size_t* src_shape, int src
         if (any) {
             std::size_t csz = 1;
             for (int i = 0; i < src_rank; ++i) csz *= c_tgt[i];
+            // When every such dim lies outside the others (a leading
+            // replication: the target is rep consecutive copies of the
+            // compact block), reduce straight into the first copy and let a
+            // small reduction write the copies itself; else broadcast.
+            bool leading = true, seen_other = false;
+            for (int i = 0; i < src_rank; ++i) {
+                if (full_tgt[i] == 1) continue;
+                if (c_tgt[i] == 1) leading = leading && !seen_other;
+                else seen_other = true;
+            }
+            const unsigned long long rep = outsz / csz;
+            if (leading) {
+                const unsigned long long ask = rep * csz <= kReplicateMax ? rep : 1;
+                const bool all = launch_vjp_reduce<F>(ops, c_src, src_rank, c_tgt, src_rank, out, divisor, nullptr, ask) &&
+                                 ask == rep;
+                if (!all) {
+                    const unsigned long long total4 = (rep - 1) * csz / 4;
+                    if (csz % 4 == 0 && aligned16(out) && total4 < (1ull << 32)) {
+                        replicate_front_block<<<grid_for(total4, kThreads), kThreads, 0, stream()>>>(
+                            out, csz / 4, FastDiv(static_cast<unsigned>(csz / 4)), total4);
+                        check_launch("replicate");
+                    } else {
+                        const size_t one_shape[2] = {1, csz}, rest_shape[2] = {static_cast<size_t>(rep - 1), csz};
+                        broadcast_copy(out, one_shape, 2, out + csz, rest_shape, 2);
+                    }
+                }
+                return true;
+            }
             Scratch compact(csz * sizeof(float));
             launch_vjp_reduce<F>(ops, c_src, src_rank, c_tgt, src_rank, compact.as<float>(), divisor);
             broadcast_copy(compact.as<float>(), c_tgt, src_rank, out, full_tgt, src_rank);
-            return;
+            return true;
         }
     }
     // 2. merge neighbours of the same class that are contiguous for every operand.
@@ -493,7 +688,7 @@ static void launch_vjp_reduce(const Src ops[3], const size_t* src_shape, int src
         }
         dims[nd++] = cur;
     }
-    if (outsz == 0) return;
+    if (outsz == 0) return true;
     RedDesc d{};
     d.divisor = divisor;
     d.out_d = out_d;
@@ -524,30 +719,46 @@ static void launch_vjp_reduce(const Src ops[3], const size_t* src_shape, int src
             for (int i = 0; i < d.nk; ++i) vec = vec && d.ks[k][i] % 4 == 0;
             for (int i = 0; i < d.nr; ++i) vec = vec && d.rs[k][i] % 4 == 0;
         }
+        if (d.nk == 0 && d.nr == 1 && d.R <= kSlicedMaxRows && inner <= kSlicedMaxOutputs && (!out_d || rep == 1)) {
+            reduce_col_sliced<F><<<static_cast<unsigned>((inner + 31) / 32), kSliceThreads, 0, stream()>>>(
+                ops[0].ptr, ops[1].ptr, ops[2].ptr, d, out, rep);
+            check_launch("reduce_col_sliced");
+            return true;
+        }
         const unsigned V = vec ? 4 : 1;
         const unsigned long long lanes = (inner + V - 1) / V;
         const unsigned long long threads_now = lanes * d.K;
         unsigned long long S = (kTargetThreads + threads_now - 1) / threads_now;
         S = std::min<unsigned long long>(S, (d.R + kMinSegment - 1) / kMinSegment);
         S = std::max<unsigned long long>(S, 1);
-        S = std::min<unsigned long long>(S, 4096);
+        S = std::min<unsigned long long>(S, kMaxSumSegments);
         d.seg = (d.R + S - 1) / S;
         d.S = static_cast<unsigned>((d.R + d.seg - 1) / d.seg);
         dim3 grid(static_cast<unsigned>((lanes + kThreads - 1) / kThreads),
                   static_cast<unsigned>(std::min<unsigned long long>(d.K, 65535)), d.S);
         if (grid.x > 0x7fffffffu) fail(VC_ERR_OVERFLOW, "reduction inner run too long");
         Scratch partial(d.S > 1 ? static_cast<std::size_t>(d.S) * d.K * d.inner * sizeof(double) : 8);
-        if (vec && d.nk == 0 && d.nr == 1)
+        const bool g_const = d.is[0] == 0 && d.rs[0][0] == 0;  // operand 0 is one value (a 0-d gradient)
+        if (vec && d.nk == 0 && d.nr == 1 && g_const && operands<F>() > 1)
+            reduce_col_simple<F, true><<<grid, kThreads, 0, stream()>>>(ops[0].ptr, ops[1].ptr, ops[2].ptr, d, out, partial.as<double>());
+        else if (vec && d.nk == 0 && d.nr == 1)
             reduce_col_simple<F><<<grid, kThreads, 0, stream()>>>(ops[0].ptr, ops[1].ptr, ops[2].ptr, d, out, partial.as<double>());
         else if (vec) reduce_col_kernel<F, true><<<grid, kThreads, 0, stream()>>>(ops[0].ptr, ops[1].ptr, ops[2].ptr, d, out, partial.as<double>());
         else reduce_col_kernel<F, false><<<grid, kThreads, 0, stream()>>>(ops[0].ptr, ops[1].ptr, ops[2].ptr, d, out, partial.as<double>());
         check_launch("reduce_col");
         if (d.S > 1) {
             const unsigned long long count = d.K * d.inner;
+            // shape-only choice: the order of the additions is part of the result
+            if (d.S >= 2 * kSlices && count <= kSlicedMaxOutputs) {
+                reduce_col_finish_sliced<<<static_cast<unsigned>((count + 31) / 32), kSliceThreads, 0, stream()>>>(
+                    partial.as<double>(), d.S, count, divisor, out, out_d, out_d ? 1 : rep);
+                check_launch("reduce_col_finish");
+                return true;
+            }
             reduce_col_finish<<<grid_for(count, kThreads), kThreads, 0, stream()>>>(partial.as<double>(), d.S, count, divisor, out, out_d);
             check_launch("reduce_col_finish");
         }
-        return;
+        return rep == 1;
     }
     // ROW: innermost reduced run.
     const unsigned long long inner = dims[nd - 1].size;
@@ -594,16 +805,17 @@ static void launch_vjp_reduce(const Src ops[3], const size_t* src_shape, int src
                             kThreads, 0, stream()>>>(partial.as<double>(), d.S, d.K, divisor, out, out_d);
         check_launch("reduce_row_finish");
     }
+    return rep == 1;
 }
 
 static void vjp_reduce(int f, const Src ops[3], const size_t* src_shape, int src_rank, const size_t* t_shape,
                        int t_rank, float* out, float divisor = 0.0f, double* out_d = nullptr) {
     switch (f) {
-        case V_G: return launch_vjp_reduce<V_G>(ops, src_shape, src_rank, t_shape, t_rank, out, divisor, out_d);
-        case V_NEG: return launch_vjp_reduce<V_NEG>(ops, src_shape, src_rank, t_shape, t_rank, out, divisor, out_d);
-        case V_MUL: return launch_vjp_reduce<V_MUL>(ops, src_shape, src_rank, t_shape, t_rank, out, divisor, out_d);
-        case V_DIV_A: return launch_vjp_reduce<V_DIV_A>(ops, src_shape, src_rank, t_shape, t_rank, out, divisor, out_d);
-        default: return launch_vjp_reduce<V_DIV_B>(ops, src_shape, src_rank, t_shape, t_rank, out, divisor, out_d);
+        case V_G: launch_vjp_reduce<V_G>(ops, src_shape, src_rank, t_shape, t_rank, out, divisor, out_d); return;
+        case V_NEG: launch_vjp_reduce<V_NEG>(ops, src_shape, src_rank, t_shape, t_rank, out, divisor, out_d); return;
+        case V_MUL: launch_vjp_reduce<V_MUL>(ops, src_shape, src_rank, t_shape, t_rank, out, divisor, out_d); return;
+        case V_DIV_A: launch_vjp_reduce<V_DIV_A>(ops, src_shape, src_rank, t_shape, t_rank, out, divisor, out_d); return;
+        default: launch_vjp_reduce<V_DIV_B>(ops, src_shape, src_rank, t_shape, t_rank, out, divisor, out_d); return;
     }
 }
 

@@ -129,6 +129,32 @@ __device__ __forceinline__ void st4_stream(float* p, float4 v) { __stcs(reinterp
 // hung kernel.
 // ---------------------------------------------------------------------------
 
+// Programmatic dependent launch. A kernel launched by launch_pdl may begin
+// while the kernel before it on the stream is still finishing (its launch and
+// CTA set-up overlap that kernel's tail). pdl_wait() blocks until every
+// earlier kernel has completed and its writes are visible -- call it before
+// the first global read or write; for a normal launch it returns at once.
+// pdl_trigger() lets the next programmatic launch start scheduling its CTAs.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, std::size_t smem, cudaStream_t s,
+                       Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+    if (err != cudaSuccess) throw std::runtime_error(std::string("cudaLaunchKernelEx: ") + cudaGetErrorString(err));
+}
+
 __device__ __forceinline__ unsigned smem_addr(const void* p) {
     return static_cast<unsigned>(__cvta_generic_to_shared(p));
 }
