@@ -38,6 +38,7 @@ constexpr unsigned kSliceThreads = 1024;               // sliced kernels: 32 out
 constexpr unsigned kSlices = kSliceThreads / 32;
 constexpr unsigned long long kSlicedMaxRows = 1024;    // single-launch column sums up to this many rows
 constexpr unsigned long long kSlicedMaxOutputs = 32768;
+constexpr unsigned long long kSlicedMaxElements = 1ull << 20;  // larger sums stream on float4 columns
 constexpr unsigned long long kReplicateMax = 1ull << 20;  // replicas written by the reduction itself, floats
 constexpr unsigned long long kRowTargetCtas = 4096;    // aim for this many (row, segment) CTAs
 constexpr unsigned long long kRowMinSegment = 4096;    // elements per row segment, at least
@@ -410,8 +411,8 @@ replicate_front_block(float* __restrict__ out, unsigned long long n4, FastDiv n4
     }
 }
 
-// Column sums over a single reduced dim of at most kSlicedMaxRows rows and// Column sums over a single reduced dim of at most kSlicedMaxRows rows and
-// few outputs, in ONE launch (no partials, no finish): a CTA owns 32
+// Column sums over a single reduced dim of at most kSlicedMaxRows rows and// Column sums over a single reduced dim of at most kSlicedMaxRows rows, few
+// outputs and at most 2^20 terms (small, launch-bound sums), in ONE launch (no partials, no finish): a CTA owns 32
 // consecutive outputs, one per lane; warp w adds rows [w * per, (w + 1) * per)
 // of its lane's column in row order, eight rows in flight, and the 32 slice
 // sums of an output are added in slice order (an order fixed by R alone).
@@ -719,7 +720,8 @@ static bool launch_vjp_reduce(const Src ops[3], const size_t* src_shape, int src
             for (int i = 0; i < d.nk; ++i) vec = vec && d.ks[k][i] % 4 == 0;
             for (int i = 0; i < d.nr; ++i) vec = vec && d.rs[k][i] % 4 == 0;
         }
-        if (d.nk == 0 && d.nr == 1 && d.R <= kSlicedMaxRows && inner <= kSlicedMaxOutputs && (!out_d || rep == 1)) {
+        if (d.nk == 0 && d.nr == 1 && d.R <= kSlicedMaxRows && inner <= kSlicedMaxOutputs &&
+            d.R * inner <= kSlicedMaxElements && (!out_d || rep == 1)) {
             reduce_col_sliced<F><<<static_cast<unsigned>((inner + 31) / 32), kSliceThreads, 0, stream()>>>(
                 ops[0].ptr, ops[1].ptr, ops[2].ptr, d, out, rep);
             check_launch("reduce_col_sliced");

@@ -34,8 +34,10 @@
 //     dx = dp * onehot + ((dl / s) + 0) * expf(x - m) with dl = sum(-dp*onehot).
 // The reference sums in double. Here the staged (TMA) paths add each group of
 // four terms in float and the group sums in double, and the exp terms of s
-// come from exp_sum_term (ex2-based, a few ulps) rather than expf; every
-// per-element output still uses expf. Results therefore differ from the CPU
+// come from exp_sum_term / exp_term (ex2-based) rather than expf; the
+// per-element outputs use expf, except the re-read kernel's softmax forward
+// and softmax backward, which use exp_sfu (within 2e-6 relative of e^t for
+// |t| <= 20). Results therefore differ from the CPU
 // path only through exp/log ulps and the order and grouping of the additions,
 // all far inside the 1e-5 sum tolerance.
 #include "vc_internal.cuh"
@@ -98,6 +100,25 @@ __device__ __forceinline__ float exp_sum_term(float x) {
     asm("max.NaN.f32 %0, %1, %2;" : "=f"(xc) : "f"(x), "f"(-110.0f));
     float e;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(xc * kL2e));
+    return e;
+}
+
+// e^t for per-element outputs on the SFU: 2^(t * log2 e), the product
+// rounded to float. The rounding perturbs the result by at most
+// |t| * 2^-24 * log2(e) * ln 2 relative (1.2e-6 at |t| = 20, 4.8e-6 at 80,
+// where e^t < 2e-35), plus ex2.approx's 2 ulp; subnormal results are kept,
+// e^-inf = 0, e^+inf = inf, NaN stays NaN. Four instructions per element
+// where expf takes about ten: the softmax outputs and the softmax backward
+// evaluate one to three of these per element and are issue-bound otherwise.
+__device__ __forceinline__ float exp_sfu(float t) {
+    float e;
+    asm("ex2.approx.f32 %0, %1;" : "=f"(e) : "f"(t * kL2e));
+    return e;
+}
+// 2^(t log2 e) for row-sum terms, subnormal results flushed to zero.
+__device__ __forceinline__ float exp_term(float t) {
+    float e;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(t * kL2e));
     return e;
 }
 
@@ -971,21 +992,15 @@ row_reread_kernel(const RowArgs a, unsigned wlog2) {
 
         // ---------------- pass 1 ----------------
         if constexpr (FWD) {
+            // Online (max, sum of e^(x - max)) per thread, one round of D
+            // float4 at a time: the round's maximum first (NaN never wins,
+            // the positions past the row end count as -inf), one rescale of
+            // the running sum when it grows, then the round's 4D terms
+            // e^(x - m) added in float by float4 and across the round, the
+            // round's total in double.
             float m = -INFINITY;
             double s = 0.0;
             bool nan_seen = false;
-            auto take = [&](const float4& v) {
-                const float mx = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
-                if (mx > m) {  // NaN never compares greater
-                    if (m != -INFINITY) s *= static_cast<double>(expf(m - mx));
-                    m = mx;
-                }
-                if (m == -INFINITY)
-                    nan_seen = nan_seen || v.x != v.x || v.y != v.y || v.z != v.z || v.w != v.w;
-                else
-                    s += quad_sum(make_float4(exp_sum_term(v.x - m), exp_sum_term(v.y - m), exp_sum_term(v.z - m),
-                                              exp_sum_term(v.w - m)));
-            };
             if (active) {
                 for (unsigned j = gt; j < L4; j += D * GT) {
                     float4 v[D];
@@ -993,7 +1008,27 @@ row_reread_kernel(const RowArgs a, unsigned wlog2) {
                     for (unsigned k = 0; k < D; ++k) v[k] = ld4_hint(xr + min(j + k * GT, L4 - 1), keep);
 #pragma unroll
                     for (unsigned k = 0; k < D; ++k)
-                        if (j + k * GT < L4) take(v[k]);
+                        if (j + k * GT >= L4) v[k] = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+                    float bm = -INFINITY;
+#pragma unroll
+                    for (unsigned k = 0; k < D; ++k)
+                        bm = fmaxf(bm, fmaxf(fmaxf(v[k].x, v[k].y), fmaxf(v[k].z, v[k].w)));
+                    if (bm > m) {  // NaN never compares greater
+                        if (m != -INFINITY) s *= static_cast<double>(expf(m - bm));
+                        m = bm;
+                    }
+                    if (m == -INFINITY) {  // nothing but -inf (and NaN) so far: no terms yet
+#pragma unroll
+                        for (unsigned k = 0; k < D; ++k)
+                            nan_seen = nan_seen || v[k].x != v[k].x || v[k].y != v[k].y || v[k].z != v[k].z ||
+                                       v[k].w != v[k].w;
+                    } else {
+                        float r = 0.0f;
+#pragma unroll
+                        for (unsigned k = 0; k < D; ++k)
+                            r += (exp_term(v[k].x - m) + exp_term(v[k].y - m)) + (exp_term(v[k].z - m) + exp_term(v[k].w - m));
+                        s += static_cast<double>(r);
+                    }
                 }
             }
             const float mw = warp_fmax(m);
@@ -1021,8 +1056,8 @@ row_reread_kernel(const RowArgs a, unsigned wlog2) {
                                 part += quad_sum(neg4(g[k]));
                             } else {
                                 const float4 gv = g[k], xv = x[k];
-                                part += quad_sum(make_float4(-(gv.x * expf((xv.x - m) - l)), -(gv.y * expf((xv.y - m) - l)),
-                                                             -(gv.z * expf((xv.z - m) - l)), -(gv.w * expf((xv.w - m) - l))));
+                                part += quad_sum(make_float4(-(gv.x * exp_sfu((xv.x - m) - l)), -(gv.y * exp_sfu((xv.y - m) - l)),
+                                                             -(gv.z * exp_sfu((xv.z - m) - l)), -(gv.w * exp_sfu((xv.w - m) - l))));
                             }
                         }
                 }
@@ -1054,7 +1089,7 @@ row_reread_kernel(const RowArgs a, unsigned wlog2) {
             }
             auto f = [&](float v) {
                 const float ls = (v - m) - l;
-                return MODE == SM_FWD ? expf(ls) : ls;
+                return MODE == SM_FWD ? exp_sfu(ls) : ls;
             };
             // ---------------- pass 2 ----------------
             for (unsigned j = gt; j < L4; j += D * GT) {
@@ -1075,8 +1110,10 @@ row_reread_kernel(const RowArgs a, unsigned wlog2) {
             // LSM_BWD: dx = g + de * expf(x - m)
             // SM_BWD:  dx = gy + de * expf(x - m), gy = g * expf((x - m) - l)
             auto f = [&](float g, float x) {
-                const float gy = MODE == SM_BWD ? g * expf((x - m) - l) : g;
-                return gy + de * expf(x - m);
+                // softmax: three exponentials per element on the SFU; log_softmax
+                // (one, and at the HBM roofline) keeps expf
+                const float gy = MODE == SM_BWD ? g * exp_sfu((x - m) - l) : g;
+                return gy + de * (MODE == SM_BWD ? exp_sfu(x - m) : expf(x - m));
             };
             // ---------------- pass 2 ----------------
             for (unsigned j = gt; j < L4; j += D * GT) {
