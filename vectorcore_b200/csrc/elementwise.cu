@@ -74,7 +74,7 @@ __device__ __forceinline__ float4 bop4(float4 x, float4 y) {
 }
 
 constexpr unsigned kThreads = 256;
-constexpr int kUnroll = 4;
+static_assert(kThreads == kStreamThreads, "the flat kernels launch stream_grid CTAs of kStreamThreads");
 
 // ---------------------------------------------------------------------------
 // Flat binary: MODE 0 same shape, 1 scalar rhs, 2 scalar lhs. The scalar is
@@ -86,32 +86,30 @@ __global__ void __launch_bounds__(kThreads)
 binary_flat_kernel(const float* __restrict__ a, const float* __restrict__ b,
                    float* __restrict__ out, std::size_t n, const float* __restrict__ sp, float sv) {
     const float s = sp ? __ldg(sp) : sv;
-    const std::size_t tid = static_cast<std::size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    const std::size_t stride = static_cast<std::size_t>(gridDim.x) * blockDim.x;
-    if constexpr (VEC) {
+    if constexpr (VEC) {  // chunked stream (stream_grid)
         const std::size_t n4 = n >> 2;
         const float4 s4 = make_float4(s, s, s, s);
-        std::size_t i = tid;
-        for (; i + (kUnroll - 1) * stride < n4; i += kUnroll * stride) {
-            float4 x[kUnroll], y[kUnroll];
+        const std::size_t base = static_cast<std::size_t>(blockIdx.x) * kChunk4 + threadIdx.x;
+        float4 x[kStreamRounds], y[kStreamRounds];
 #pragma unroll
-            for (int u = 0; u < kUnroll; ++u) {
-                const std::size_t k = (i + u * stride) * 4;
-                x[u] = MODE == 2 ? s4 : ld4_stream(a + k);
-                y[u] = MODE == 1 ? s4 : ld4_stream(b + k);
+        for (unsigned u = 0; u < kStreamRounds; ++u) {
+            const std::size_t k = base + u * kStreamThreads;
+            if (k < n4) {
+                x[u] = MODE == 2 ? s4 : ldg4(a + 4 * k);
+                y[u] = MODE == 1 ? s4 : ldg4(b + 4 * k);
             }
+        }
 #pragma unroll
-            for (int u = 0; u < kUnroll; ++u) st4_stream(out + (i + u * stride) * 4, bop4<OP>(x[u], y[u]));
+        for (unsigned u = 0; u < kStreamRounds; ++u) {
+            const std::size_t k = base + u * kStreamThreads;
+            if (k < n4) st4(out + 4 * k, bop4<OP>(x[u], y[u]));
         }
-        for (; i < n4; i += stride) {
-            const std::size_t k = i * 4;
-            const float4 x = MODE == 2 ? s4 : ld4_stream(a + k);
-            const float4 y = MODE == 1 ? s4 : ld4_stream(b + k);
-            st4_stream(out + k, bop4<OP>(x, y));
-        }
-        for (std::size_t k = n4 * 4 + tid; k < n; k += stride)
-            out[k] = bop<OP>(MODE == 2 ? s : a[k], MODE == 1 ? s : b[k]);
+        if (blockIdx.x == gridDim.x - 1)
+            for (std::size_t k = n4 * 4 + threadIdx.x; k < n; k += kStreamThreads)
+                out[k] = bop<OP>(MODE == 2 ? s : a[k], MODE == 1 ? s : b[k]);
     } else {
+        const std::size_t tid = static_cast<std::size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+        const std::size_t stride = static_cast<std::size_t>(gridDim.x) * blockDim.x;
         for (std::size_t k = tid; k < n; k += stride)
             out[k] = bop<OP>(MODE == 2 ? s : a[k], MODE == 1 ? s : b[k]);
     }
@@ -389,26 +387,25 @@ binary_splat_kernel(const float* __restrict__ ap, float av, const float* __restr
 template <int OP, bool VEC>
 __global__ void __launch_bounds__(kThreads)
 unary_kernel(const float* __restrict__ in, float* __restrict__ out, std::size_t n) {
-    const std::size_t tid = static_cast<std::size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    const std::size_t stride = static_cast<std::size_t>(gridDim.x) * blockDim.x;
-    if constexpr (VEC) {
+    if constexpr (VEC) {  // chunked stream (stream_grid)
         const std::size_t n4 = n >> 2;
-        std::size_t i = tid;
-        for (; i + (kUnroll - 1) * stride < n4; i += kUnroll * stride) {
-            float4 x[kUnroll];
+        const std::size_t base = static_cast<std::size_t>(blockIdx.x) * kChunk4 + threadIdx.x;
+        float4 x[kStreamRounds];
 #pragma unroll
-            for (int u = 0; u < kUnroll; ++u) x[u] = ld4_stream(in + (i + u * stride) * 4);
+        for (unsigned u = 0; u < kStreamRounds; ++u) {
+            const std::size_t k = base + u * kStreamThreads;
+            if (k < n4) x[u] = ldg4(in + 4 * k);
+        }
 #pragma unroll
-            for (int u = 0; u < kUnroll; ++u)
-                st4_stream(out + (i + u * stride) * 4,
-                           make_float4(uop<OP>(x[u].x), uop<OP>(x[u].y), uop<OP>(x[u].z), uop<OP>(x[u].w)));
+        for (unsigned u = 0; u < kStreamRounds; ++u) {
+            const std::size_t k = base + u * kStreamThreads;
+            if (k < n4) st4(out + 4 * k, make_float4(uop<OP>(x[u].x), uop<OP>(x[u].y), uop<OP>(x[u].z), uop<OP>(x[u].w)));
         }
-        for (; i < n4; i += stride) {
-            const float4 x = ld4_stream(in + i * 4);
-            st4_stream(out + i * 4, make_float4(uop<OP>(x.x), uop<OP>(x.y), uop<OP>(x.z), uop<OP>(x.w)));
-        }
-        for (std::size_t k = n4 * 4 + tid; k < n; k += stride) out[k] = uop<OP>(in[k]);
+        if (blockIdx.x == gridDim.x - 1)
+            for (std::size_t k = n4 * 4 + threadIdx.x; k < n; k += kStreamThreads) out[k] = uop<OP>(in[k]);
     } else {
+        const std::size_t tid = static_cast<std::size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+        const std::size_t stride = static_cast<std::size_t>(gridDim.x) * blockDim.x;
         for (std::size_t k = tid; k < n; k += stride) out[k] = uop<OP>(in[k]);
     }
 }
@@ -420,38 +417,33 @@ unary_backward_kernel(const float* __restrict__ x, const float* __restrict__ y,
                       const float* __restrict__ g, float* __restrict__ dx, std::size_t n) {
     constexpr bool NEED_X = OP == VC_LOG || OP == VC_RELU;
     constexpr bool NEED_Y = OP == VC_EXP || OP == VC_SIGMOID;
-    const std::size_t tid = static_cast<std::size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    const std::size_t stride = static_cast<std::size_t>(gridDim.x) * blockDim.x;
-    if constexpr (VEC) {
+    if constexpr (VEC) {  // chunked stream (stream_grid)
         const std::size_t n4 = n >> 2;
-        std::size_t i = tid;
+        const std::size_t base = static_cast<std::size_t>(blockIdx.x) * kChunk4 + threadIdx.x;
         const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (; i + (kUnroll - 1) * stride < n4; i += kUnroll * stride) {
-            float4 gx[kUnroll], xx[kUnroll], yy[kUnroll];
+        float4 gx[kStreamRounds], xx[kStreamRounds], yy[kStreamRounds];
 #pragma unroll
-            for (int u = 0; u < kUnroll; ++u) {
-                const std::size_t k = (i + u * stride) * 4;
-                gx[u] = ld4_stream(g + k);
-                xx[u] = NEED_X ? ld4_stream(x + k) : z;
-                yy[u] = NEED_Y ? ld4_stream(y + k) : z;
+        for (unsigned u = 0; u < kStreamRounds; ++u) {
+            const std::size_t k = base + u * kStreamThreads;
+            if (k < n4) {
+                gx[u] = ldg4(g + 4 * k);
+                xx[u] = NEED_X ? ldg4(x + 4 * k) : z;
+                yy[u] = NEED_Y ? ldg4(y + 4 * k) : z;
             }
+        }
 #pragma unroll
-            for (int u = 0; u < kUnroll; ++u)
-                st4_stream(dx + (i + u * stride) * 4,
-                           make_float4(ubwd<OP>(xx[u].x, yy[u].x, gx[u].x), ubwd<OP>(xx[u].y, yy[u].y, gx[u].y),
-                                       ubwd<OP>(xx[u].z, yy[u].z, gx[u].z), ubwd<OP>(xx[u].w, yy[u].w, gx[u].w)));
+        for (unsigned u = 0; u < kStreamRounds; ++u) {
+            const std::size_t k = base + u * kStreamThreads;
+            if (k < n4)
+                st4(dx + 4 * k, make_float4(ubwd<OP>(xx[u].x, yy[u].x, gx[u].x), ubwd<OP>(xx[u].y, yy[u].y, gx[u].y),
+                                            ubwd<OP>(xx[u].z, yy[u].z, gx[u].z), ubwd<OP>(xx[u].w, yy[u].w, gx[u].w)));
         }
-        for (; i < n4; i += stride) {
-            const std::size_t k = i * 4;
-            const float4 gv = ld4_stream(g + k);
-            const float4 xv = NEED_X ? ld4_stream(x + k) : z;
-            const float4 yv = NEED_Y ? ld4_stream(y + k) : z;
-            st4_stream(dx + k, make_float4(ubwd<OP>(xv.x, yv.x, gv.x), ubwd<OP>(xv.y, yv.y, gv.y),
-                                           ubwd<OP>(xv.z, yv.z, gv.z), ubwd<OP>(xv.w, yv.w, gv.w)));
-        }
-        for (std::size_t k = n4 * 4 + tid; k < n; k += stride)
-            dx[k] = ubwd<OP>(NEED_X ? x[k] : 0.f, NEED_Y ? y[k] : 0.f, g[k]);
+        if (blockIdx.x == gridDim.x - 1)
+            for (std::size_t k = n4 * 4 + threadIdx.x; k < n; k += kStreamThreads)
+                dx[k] = ubwd<OP>(NEED_X ? x[k] : 0.f, NEED_Y ? y[k] : 0.f, g[k]);
     } else {
+        const std::size_t tid = static_cast<std::size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+        const std::size_t stride = static_cast<std::size_t>(gridDim.x) * blockDim.x;
         for (std::size_t k = tid; k < n; k += stride)
             dx[k] = ubwd<OP>(NEED_X ? x[k] : 0.f, NEED_Y ? y[k] : 0.f, g[k]);
     }
@@ -618,7 +610,7 @@ static void launch_binary_op(const Operand& a, const Operand& b, float* out, con
     else if (b.ptr && b_flat && a_scalar) mode = 2;
     if (mode >= 0) {
         const bool vec = aligned16(out) && (mode == 2 || aligned16(a.ptr)) && (mode == 1 || aligned16(b.ptr));
-        const unsigned grid = grid_for(vec ? (n + 3) / 4 : n, kThreads);
+        const unsigned grid = vec ? stream_grid(n) : grid_for(n, kThreads);
         const float* sp = mode == 1 ? b.ptr : (mode == 2 ? a.ptr : nullptr);
         const float sv = mode == 1 ? b.value : a.value;
 #define VC_FLAT(M, V) binary_flat_kernel<OP, M, V><<<grid, kThreads, 0, s>>>(a.ptr, b.ptr, out, n, sp, sv)
@@ -731,7 +723,7 @@ void broadcast_copy(const float* src, const size_t* src_shape, int src_rank, flo
 template <int OP>
 static void launch_unary_op(const float* in, float* out, std::size_t n) {
     const bool vec = aligned16(in) && aligned16(out);
-    const unsigned grid = grid_for(vec ? (n + 3) / 4 : n, kThreads);
+    const unsigned grid = vec ? stream_grid(n) : grid_for(n, kThreads);
     if (vec) unary_kernel<OP, true><<<grid, kThreads, 0, stream()>>>(in, out, n);
     else unary_kernel<OP, false><<<grid, kThreads, 0, stream()>>>(in, out, n);
     check_launch("unary");
@@ -743,7 +735,7 @@ static void launch_unary_backward_op(const float* x, const float* y, const float
     constexpr bool NEED_Y = OP == VC_EXP || OP == VC_SIGMOID;
     if ((NEED_X && !x) || (NEED_Y && !y)) fail(VC_ERR_INVALID, "unary_backward: the saved tensor this rule needs is null");
     const bool vec = aligned16(g) && aligned16(dx) && (!NEED_X || aligned16(x)) && (!NEED_Y || aligned16(y));
-    const unsigned grid = grid_for(vec ? (n + 3) / 4 : n, kThreads);
+    const unsigned grid = vec ? stream_grid(n) : grid_for(n, kThreads);
     if (vec) unary_backward_kernel<OP, true><<<grid, kThreads, 0, stream()>>>(x, y, g, dx, n);
     else unary_backward_kernel<OP, false><<<grid, kThreads, 0, stream()>>>(x, y, g, dx, n);
     check_launch("unary_backward");

@@ -841,44 +841,42 @@ __device__ __forceinline__ void bb_four(const float4& av, const float4& bv, cons
     bb_one<OP>(av.w, bv.w, gv.w, ga.w, gb.w);
 }
 
-// Two float4 of each input in flight per thread per iteration; at most 64
-// registers so four CTAs stay resident per SM.
+// Chunked stream (stream_grid): CTA b owns float4 groups
+// [kChunk4 * b, kChunk4 * (b + 1)), four per thread, all loads first.
 template <int OP, bool VEC>
-__global__ void __launch_bounds__(kThreads, 4)
+__global__ void __launch_bounds__(kThreads)
 binary_backward_flat(const float* __restrict__ a, const float* __restrict__ b, const float* __restrict__ g,
                      float* __restrict__ da, float* __restrict__ db, std::size_t n) {
-    const std::size_t stride = static_cast<std::size_t>(gridDim.x) * blockDim.x;
-    const std::size_t tid = static_cast<std::size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     constexpr bool NEED_AB = OP == VC_MUL || OP == VC_DIV;
     if constexpr (VEC) {
         const std::size_t n4 = n >> 2;
-        std::size_t i = tid;
-        for (; i + stride < n4; i += 2 * stride) {
-            const std::size_t k0 = i * 4, k1 = (i + stride) * 4;
-            const float4 g0 = ld4_stream(g + k0), g1 = ld4_stream(g + k1);
-            const float4 a0 = NEED_AB ? ld4_stream(a + k0) : g0, a1 = NEED_AB ? ld4_stream(a + k1) : g1;
-            const float4 b0 = NEED_AB ? ld4_stream(b + k0) : g0, b1 = NEED_AB ? ld4_stream(b + k1) : g1;
-            float4 ga0, gb0, ga1, gb1;
-            bb_four<OP>(a0, b0, g0, ga0, gb0);
-            bb_four<OP>(a1, b1, g1, ga1, gb1);
-            st4_stream(da + k0, ga0);
-            st4_stream(db + k0, gb0);
-            st4_stream(da + k1, ga1);
-            st4_stream(db + k1, gb1);
+        const std::size_t base = static_cast<std::size_t>(blockIdx.x) * kChunk4 + threadIdx.x;
+        float4 gv[kStreamRounds], av[kStreamRounds], bv[kStreamRounds];
+#pragma unroll
+        for (unsigned u = 0; u < kStreamRounds; ++u) {
+            const std::size_t k = base + u * kStreamThreads;
+            if (k < n4) {
+                gv[u] = ldg4(g + 4 * k);
+                av[u] = NEED_AB ? ldg4(a + 4 * k) : gv[u];
+                bv[u] = NEED_AB ? ldg4(b + 4 * k) : gv[u];
+            }
         }
-        for (; i < n4; i += stride) {
-            const std::size_t k = i * 4;
-            const float4 gv = ld4_stream(g + k);
-            const float4 av = NEED_AB ? ld4_stream(a + k) : gv;
-            const float4 bv = NEED_AB ? ld4_stream(b + k) : gv;
-            float4 ga, gb;
-            bb_four<OP>(av, bv, gv, ga, gb);
-            st4_stream(da + k, ga);
-            st4_stream(db + k, gb);
+#pragma unroll
+        for (unsigned u = 0; u < kStreamRounds; ++u) {
+            const std::size_t k = base + u * kStreamThreads;
+            if (k < n4) {
+                float4 ga, gb;
+                bb_four<OP>(av[u], bv[u], gv[u], ga, gb);
+                st4(da + 4 * k, ga);
+                st4(db + 4 * k, gb);
+            }
         }
-        for (std::size_t k = n4 * 4 + tid; k < n; k += stride)
-            bb_one<OP>(NEED_AB ? a[k] : 0.f, NEED_AB ? b[k] : 0.f, g[k], da[k], db[k]);
+        if (blockIdx.x == gridDim.x - 1)
+            for (std::size_t k = n4 * 4 + threadIdx.x; k < n; k += kStreamThreads)
+                bb_one<OP>(NEED_AB ? a[k] : 0.f, NEED_AB ? b[k] : 0.f, g[k], da[k], db[k]);
     } else {
+        const std::size_t stride = static_cast<std::size_t>(gridDim.x) * blockDim.x;
+        const std::size_t tid = static_cast<std::size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
         for (std::size_t k = tid; k < n; k += stride)
             bb_one<OP>(NEED_AB ? a[k] : 0.f, NEED_AB ? b[k] : 0.f, g[k], da[k], db[k]);
     }
@@ -1727,7 +1725,8 @@ vc_status vc_cuda_binary_backward(int op, const float* a, const size_t* a_shape,
     };
     if (da && db && same(a_shape, a_rank) && same(b_shape, b_rank) && same(g_shape, g_rank)) {
         const bool vec = aligned16(a) && aligned16(b) && aligned16(g) && aligned16(da) && aligned16(db);
-        const unsigned grid = grid_for(vec ? (n + 3) / 4 : n, kThreads);
+        static_assert(kThreads == kStreamThreads, "binary_backward_flat launches stream_grid CTAs");
+        const unsigned grid = vec ? stream_grid(n) : grid_for(n, kThreads);
 #define VC_BB(OP) do { if (vec) binary_backward_flat<OP, true><<<grid, kThreads, 0, stream()>>>(a, b, g, da, db, n); \
                        else binary_backward_flat<OP, false><<<grid, kThreads, 0, stream()>>>(a, b, g, da, db, n); } while (0)
         switch (op) {

@@ -106,13 +106,15 @@ __device__ __forceinline__ float exp_sum_term(float x) {
 // e^t for per-element outputs on the SFU: 2^(t * log2 e), the product
 // rounded to float. The rounding perturbs the result by at most
 // |t| * 2^-24 * log2(e) * ln 2 relative (1.2e-6 at |t| = 20, 4.8e-6 at 80,
-// where e^t < 2e-35), plus ex2.approx's 2 ulp; subnormal results are kept,
-// e^-inf = 0, e^+inf = inf, NaN stays NaN. Four instructions per element
-// where expf takes about ten: the softmax outputs and the softmax backward
-// evaluate one to three of these per element and are issue-bound otherwise.
+// where e^t < 2e-35), plus ex2.approx's 2 ulp; results below 2^-126 flush
+// to zero (an absolute error under 1.2e-38), e^-inf = 0, e^+inf = inf, NaN
+// stays NaN. Two instructions per element where expf takes about ten: the
+// softmax outputs and the softmax backward evaluate one to three of these
+// per element and are issue-bound otherwise (keeping subnormal results costs
+// softmax's forward 4 points of HBM bandwidth).
 __device__ __forceinline__ float exp_sfu(float t) {
     float e;
-    asm("ex2.approx.f32 %0, %1;" : "=f"(e) : "f"(t * kL2e));
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(t * kL2e));
     return e;
 }
 // 2^(t log2 e) for row-sum terms, subnormal results flushed to zero.
