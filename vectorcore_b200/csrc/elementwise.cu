@@ -369,16 +369,22 @@ __global__ void __launch_bounds__(kThreads)
 binary_splat_kernel(const float* __restrict__ ap, float av, const float* __restrict__ bp, float bv,
                     float* __restrict__ out, std::size_t n, bool vec) {
     const float v = bop<OP>(ap ? __ldg(ap) : av, bp ? __ldg(bp) : bv);
-    const std::size_t tid = static_cast<std::size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    const std::size_t stride = static_cast<std::size_t>(gridDim.x) * blockDim.x;
-    std::size_t start = 0;
-    if (vec) {
+    if (vec) {  // chunked stream (stream_grid): a write-only stream, 7.3 TB/s chunked vs 6.2 grid-stride
         const std::size_t n4 = n >> 2;
         const float4 v4 = make_float4(v, v, v, v);
-        for (std::size_t i = tid; i < n4; i += stride) st4_stream(out + i * 4, v4);
-        start = n4 * 4;
+        const std::size_t base = static_cast<std::size_t>(blockIdx.x) * kChunk4 + threadIdx.x;
+#pragma unroll
+        for (unsigned u = 0; u < kStreamRounds; ++u) {
+            const std::size_t k = base + u * kStreamThreads;
+            if (k < n4) st4(out + 4 * k, v4);
+        }
+        if (blockIdx.x == gridDim.x - 1)
+            for (std::size_t k = n4 * 4 + threadIdx.x; k < n; k += kStreamThreads) out[k] = v;
+        return;
     }
-    for (std::size_t k = start + tid; k < n; k += stride) out[k] = v;
+    const std::size_t tid = static_cast<std::size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const std::size_t stride = static_cast<std::size_t>(gridDim.x) * blockDim.x;
+    for (std::size_t k = tid; k < n; k += stride) out[k] = v;
 }
 
 // ---------------------------------------------------------------------------
@@ -626,7 +632,7 @@ static void launch_binary_op(const Operand& a, const Operand& b, float* out, con
     for (int i = 0; i < c.rank; ++i) all_zero = all_zero && c.sa[i] == 0 && c.sb[i] == 0;
     if (all_zero) {
         const bool vec = aligned16(out);
-        binary_splat_kernel<OP><<<grid_for(vec ? (n + 3) / 4 : n, kThreads), kThreads, 0, s>>>(
+        binary_splat_kernel<OP><<<vec ? stream_grid(n) : grid_for(n, kThreads), kThreads, 0, s>>>(
             a.ptr, a.value, b.ptr, b.value, out, n, vec);
         check_launch("binary_splat");
         return;

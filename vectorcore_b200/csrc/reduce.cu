@@ -46,10 +46,25 @@ constexpr unsigned long long kRowMinSegment = 4096;    // elements per row segme
 // Segments per row for a ROW-layout reduction of K rows of W elements: enough
 // (row, segment) CTAs to fill the machine, each at least kRowMinSegment long.
 // A function of the shape only.
+// Few outputs (a full sum or max): aim for 16384 segments of at least 16384
+// elements -- 64 KiB pieces, the read-only stream's sweet spot (1 GiB:
+// 7.1 TB/s in 64 KiB pieces, 6.9 in 256 KiB ones) -- and finish the
+// partials with 1024 threads per output.
+constexpr unsigned long long kRowFewOutputs = 64;
+constexpr unsigned long long kRowFewTargetCtas = 16384;
+constexpr unsigned long long kRowFewMinSegment = 16384;
+constexpr unsigned kFinishWideThreads = 1024;
 inline unsigned long long row_segments(unsigned long long K, unsigned long long W) {
-    unsigned long long S = (kRowTargetCtas + K - 1) / K;
-    S = std::min<unsigned long long>(S, (W + kRowMinSegment - 1) / kRowMinSegment);
+    const bool few = K < kRowFewOutputs;
+    unsigned long long S = ((few ? kRowFewTargetCtas : kRowTargetCtas) + K - 1) / K;
+    const unsigned long long min_seg = few ? kRowFewMinSegment : kRowMinSegment;
+    S = std::min<unsigned long long>(S, (W + min_seg - 1) / min_seg);
     return std::max<unsigned long long>(1, std::min<unsigned long long>(S, 65535));
+}
+// Threads per CTA of the row finishes: 1024 for few outputs with many
+// segments (a shape-only choice: it fixes the order of the additions).
+inline unsigned row_finish_threads(unsigned long long K, unsigned long long S) {
+    return K < kRowFewOutputs && S >= 1024 ? kFinishWideThreads : 256;
 }
 
 // Element functions of the backward rules, arithmetic exactly as written in
@@ -383,35 +398,33 @@ reduce_col_finish_sliced(const double* __restrict__ partial, unsigned S, unsigne
 
 // out[k * n + j] = out[j] for k in [1, rep): copies of the block just
 // written at the front of the same buffer (the compact result of a broadcast
-// gradient), as a store stream. Thread t of the grid owns float4 groups
-// t, t + T, ... of the copies, four in flight; the source group comes from
-// L1/L2 (the block is small and every copy reads it). n % 4 == 0 and `out`
-// 16-byte aligned; (rep - 1) * n / 4 < 2^32 (FastDiv).
+// gradient), as a chunked store stream (stream_grid: one CTA per 1024 float4
+// groups of the copies, four per thread); the source group comes from L1/L2
+// (the block is small and every copy reads it). n % 4 == 0 and `out` 16-byte
+// aligned; (rep - 1) * n / 4 < 2^32 (FastDiv).
 __global__ void __launch_bounds__(kThreads)
 replicate_front_block(float* __restrict__ out, unsigned long long n4, FastDiv n4_fd, unsigned long long total4) {
     const float4* src = reinterpret_cast<const float4*>(out);
     float4* dst = reinterpret_cast<float4*>(out) + n4;
-    const unsigned long long T = static_cast<unsigned long long>(gridDim.x) * blockDim.x;
-    unsigned long long i = static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-    for (; i + 3 * T < total4; i += 4 * T) {
-        float4 v[4];
+    const unsigned long long base = static_cast<unsigned long long>(blockIdx.x) * kChunk4 + threadIdx.x;
+    float4 v[kStreamRounds];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
+    for (unsigned u = 0; u < kStreamRounds; ++u) {
+        const unsigned long long i = base + u * kStreamThreads;
+        if (i < total4) {
             unsigned q, r;
-            n4_fd.divmod(static_cast<unsigned>(i + k * T), q, r);
-            v[k] = __ldg(src + r);
+            n4_fd.divmod(static_cast<unsigned>(i), q, r);
+            v[u] = __ldg(src + r);
         }
-#pragma unroll
-        for (int k = 0; k < 4; ++k) __stcs(dst + i + k * T, v[k]);
     }
-    for (; i < total4; i += T) {
-        unsigned q, r;
-        n4_fd.divmod(static_cast<unsigned>(i), q, r);
-        __stcs(dst + i, __ldg(src + r));
+#pragma unroll
+    for (unsigned u = 0; u < kStreamRounds; ++u) {
+        const unsigned long long i = base + u * kStreamThreads;
+        if (i < total4) dst[i] = v[u];
     }
 }
 
-// Column sums over a single reduced dim of at most kSlicedMaxRows rows and// Column sums over a single reduced dim of at most kSlicedMaxRows rows, few
+// Column sums over a single reduced dim of at most kSlicedMaxRows rows, few
 // outputs and at most 2^20 terms (small, launch-bound sums), in ONE launch (no partials, no finish): a CTA owns 32
 // consecutive outputs, one per lane; warp w adds rows [w * per, (w + 1) * per)
 // of its lane's column in row order, eight rows in flight, and the 32 slice
@@ -557,13 +570,24 @@ reduce_row_kernel(const float* __restrict__ g, const float* __restrict__ p, cons
 // t, t+256, ... and a fixed block tree combines the threads (an order that
 // depends only on S), so few outputs with many segments (a full sum) finish in
 // parallel rather than in one thread.
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kFinishWideThreads)
 reduce_row_finish(const double* __restrict__ partial, unsigned S, unsigned long long K, float divisor,
                   float* __restrict__ out, double* __restrict__ out_d) {
     __shared__ double s_red[32];
     for (unsigned long long k = blockIdx.x; k < K; k += gridDim.x) {
         double acc = 0.0;
-        for (unsigned s = threadIdx.x; s < S; s += blockDim.x) acc += partial[k * S + s];
+        // partials t, t + B, t + 2B, ... in order, eight loads in flight
+        for (unsigned s0 = threadIdx.x; s0 < S; s0 += 8 * blockDim.x) {
+            double v[8];
+#pragma unroll
+            for (unsigned j = 0; j < 8; ++j) {
+                const unsigned s = s0 + j * blockDim.x;
+                v[j] = s < S ? partial[k * S + s] : 0.0;
+            }
+#pragma unroll
+            for (unsigned j = 0; j < 8; ++j)
+                if (s0 + j * blockDim.x < S) acc += v[j];
+        }
         acc = block_sum(acc, s_red);
         if (threadIdx.x == 0) {
             if (out_d) out_d[k] = acc;
@@ -653,7 +677,7 @@ static bool launch_vjp_reduce(const Src ops[3], const size_t* src_shape, int src
                 if (!all) {
                     const unsigned long long total4 = (rep - 1) * csz / 4;
                     if (csz % 4 == 0 && aligned16(out) && total4 < (1ull << 32)) {
-                        replicate_front_block<<<grid_for(total4, kThreads), kThreads, 0, stream()>>>(
+                        replicate_front_block<<<stream_grid(4 * total4), kThreads, 0, stream()>>>(
                             out, csz / 4, FastDiv(static_cast<unsigned>(csz / 4)), total4);
                         check_launch("replicate");
                     } else {
@@ -804,7 +828,7 @@ static bool launch_vjp_reduce(const Src ops[3], const size_t* src_shape, int src
     check_launch("reduce_row");
     if (d.S > 1) {
         reduce_row_finish<<<static_cast<unsigned>(std::min<unsigned long long>(d.K, static_cast<unsigned long long>(sm_count()) * 8)),
-                            kThreads, 0, stream()>>>(partial.as<double>(), d.S, d.K, divisor, out, out_d);
+                            row_finish_threads(d.K, d.S), 0, stream()>>>(partial.as<double>(), d.S, d.K, divisor, out, out_d);
         check_launch("reduce_row_finish");
     }
     return rep == 1;
@@ -1386,7 +1410,7 @@ max_row_kernel(const float* __restrict__ in, unsigned long long outer, unsigned 
     }
 }
 
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kFinishWideThreads)
 max_row_finish(const float* __restrict__ in, unsigned long long outer, unsigned long long length, unsigned S,
                const float* __restrict__ pv, const long long* __restrict__ pi, MaxOut o) {
     // One CTA per row. max_combine (larger value, then smaller index) is
@@ -1395,8 +1419,16 @@ max_row_finish(const float* __restrict__ in, unsigned long long outer, unsigned 
     __shared__ long long s_i[32];
     for (unsigned long long row = blockIdx.x; row < outer; row += gridDim.x) {
         MaxCand c{0.0f, -1};
-        for (unsigned s = threadIdx.x; s < S; s += blockDim.x)
-            c = max_combine(c, MaxCand{pv[row * S + s], pi[row * S + s]});
+        for (unsigned s0 = threadIdx.x; s0 < S; s0 += 4 * blockDim.x) {
+            MaxCand v[4];
+#pragma unroll
+            for (unsigned j = 0; j < 4; ++j) {
+                const unsigned s = s0 + j * blockDim.x;
+                v[j] = s < S ? MaxCand{pv[row * S + s], pi[row * S + s]} : MaxCand{0.0f, -1};
+            }
+#pragma unroll
+            for (unsigned j = 0; j < 4; ++j) c = max_combine(c, v[j]);
+        }
         c = block_max(c, s_v, s_i);
         if (threadIdx.x == 0) max_finish_write(c, in[row * length], o, row);
         __syncthreads();
@@ -1493,7 +1525,7 @@ static void launch_max(const float* in, std::size_t outer, std::size_t length, s
         check_launch("max_row");
         if (Sn > 1) {
             max_row_finish<<<static_cast<unsigned>(std::min<std::size_t>(outer, static_cast<std::size_t>(sm_count()) * 8)),
-                             kThreads, 0, st>>>(in, outer, length, Sn, pv.as<float>(), pi.as<long long>(), o);
+                             row_finish_threads(outer, Sn), 0, st>>>(in, outer, length, Sn, pv.as<float>(), pi.as<long long>(), o);
             check_launch("max_row_finish");
         }
         return;
