@@ -492,6 +492,58 @@ ce_backward_kernel(const float* __restrict__ x, const long long* __restrict__ ta
     }
 }
 
+// The same dlogits over the flat [rows, classes] array as a chunked stream
+// (classes % 4 == 0, rows * classes / 4 < 2^32): CTA b owns float4 groups
+// [kChunk4 * b, kChunk4 * (b + 1)), four per thread, all loads first; a
+// group's row comes from a FastDiv by classes / 4, and the row's m, s, target
+// and de = (dl / s) + 0 are reloaded only when the row changes (at most four
+// times per thread for classes >= 1024). The exponential is
+// exp_sfu (within 2e-6 relative of expf for |x - m| <= 20).
+__global__ void __launch_bounds__(kThreads)
+ce_backward_stream(const float* __restrict__ x, const long long* __restrict__ targets,
+                   const float* __restrict__ row_max, const float* __restrict__ row_sum,
+                   const float* __restrict__ upstream, unsigned long long n4, FastDiv classes4,
+                   float batch_total, float* __restrict__ dx) {
+    const float u = __ldg(upstream);
+    const float dn = u / batch_total;
+    const float dt = -dn;
+    const float dp = dt + 0.0f;
+    float dl;
+    if (dp == 0.0f) dl = 0.0f;
+    else if (isinf(dp) && classes4.divisor * 4ull > 1) dl = __int_as_float(0x7fc00000);
+    else dl = -dp;
+    const unsigned long long base = static_cast<unsigned long long>(blockIdx.x) * kChunk4 + threadIdx.x;
+    float4 xv[kStreamRounds];
+#pragma unroll
+    for (unsigned k = 0; k < kStreamRounds; ++k) {
+        const unsigned long long i = base + k * kStreamThreads;
+        if (i < n4) xv[k] = ldg4(x + 4 * i);
+    }
+    unsigned cur = 0xffffffffu;
+    float m = 0.0f, de = 0.0f;
+    long long t = -1;
+#pragma unroll
+    for (unsigned k = 0; k < kStreamRounds; ++k) {
+        const unsigned long long i = base + k * kStreamThreads;
+        if (i >= n4) break;
+        unsigned row, c4;
+        classes4.divmod(static_cast<unsigned>(i), row, c4);
+        if (row != cur) {
+            cur = row;
+            m = __ldg(row_max + row);
+            de = (dl / __ldg(row_sum + row)) + 0.0f;
+            t = __ldg(targets + row);
+        }
+        const long long c = 4ll * c4;
+        float4 o;
+        o.x = dp * (c == t ? 1.0f : 0.0f) + de * exp_sfu(xv[k].x - m);
+        o.y = dp * (c + 1 == t ? 1.0f : 0.0f) + de * exp_sfu(xv[k].y - m);
+        o.z = dp * (c + 2 == t ? 1.0f : 0.0f) + de * exp_sfu(xv[k].z - m);
+        o.w = dp * (c + 3 == t ? 1.0f : 0.0f) + de * exp_sfu(xv[k].w - m);
+        st4(dx + 4 * i, o);
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Pipelined row kernel for 16-byte-aligned rows whose length is a multiple
 // of 4: a persistent grid of clusters, cluster k handling rows k,
@@ -1383,8 +1435,17 @@ vc_status vc_cuda_cross_entropy_backward(const float* logits, const int64_t* tar
     if (!logits || !targets || !row_max || !row_sum || !upstream || !dlogits)
         fail(VC_ERR_INVALID, "cross_entropy_backward: null pointer");
     const bool vec = classes % 4 == 0 && aligned16(logits) && aligned16(dlogits);
-    const unsigned grid = static_cast<unsigned>(std::min<std::size_t>(batch, static_cast<std::size_t>(sm_count()) * 16));
     const auto* t = reinterpret_cast<const long long*>(targets);
+    const unsigned long long n4 = static_cast<unsigned long long>(batch) * classes / 4;
+    if (vec && classes >= 1024 && n4 < (1ull << 32)) {
+        static_assert(kThreads == kStreamThreads, "ce_backward_stream launches stream_grid CTAs");
+        ce_backward_stream<<<stream_grid(4 * n4), kThreads, 0, stream()>>>(
+            logits, t, row_max, row_sum, upstream, n4, FastDiv(static_cast<unsigned>(classes / 4)),
+            static_cast<float>(batch_total), dlogits);
+        check_launch("cross_entropy_backward");
+        return VC_OK;
+    }
+    const unsigned grid = static_cast<unsigned>(std::min<std::size_t>(batch, static_cast<std::size_t>(sm_count()) * 16));
     if (vec) ce_backward_kernel<true><<<grid, kThreads, 0, stream()>>>(logits, t, row_max, row_sum, upstream, batch, classes, static_cast<float>(batch_total), dlogits);
     else ce_backward_kernel<false><<<grid, kThreads, 0, stream()>>>(logits, t, row_max, row_sum, upstream, batch, classes, static_cast<float>(batch_total), dlogits);
     check_launch("cross_entropy_backward");
