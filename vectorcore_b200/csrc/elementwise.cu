@@ -693,13 +693,14 @@ static void launch_binary_op(const Operand& a, const Operand& b, float* out, con
         rd.L4 = static_cast<unsigned>(d.L / 4);
         const std::size_t warps_per_cta = kThreads / 32;
         const std::size_t ctas = (d.rows + warps_per_cta - 1) / warps_per_cta;
-        const unsigned grid = static_cast<unsigned>(std::min<std::size_t>(ctas, static_cast<std::size_t>(sm_count()) * 16));
+        // one CTA per 8 rows, no persistent loop (short-lived CTAs stream better)
+        const unsigned grid = static_cast<unsigned>(std::min<std::size_t>(ctas, 0x7fffffffull));
         binary_rows_kernel<OP><<<grid, kThreads, 0, s>>>(a.ptr, b.ptr, out, rd, a.value, b.value);
         check_launch("binary_rows");
         return;
     }
     const std::size_t tiles = (d.rows + d.tile_rows - 1) / d.tile_rows * d.col_chunks;
-    const unsigned grid = static_cast<unsigned>(std::min<std::size_t>(tiles, static_cast<std::size_t>(sm_count()) * 8));
+    const unsigned grid = static_cast<unsigned>(std::min<std::size_t>(tiles, 0x7fffffffull));  // a CTA per tile
     if (vec) binary_tiled_kernel<OP, true><<<grid, kThreads, 0, s>>>(a.ptr, b.ptr, out, d, a.value, b.value);
     else binary_tiled_kernel<OP, false><<<grid, kThreads, 0, s>>>(a.ptr, b.ptr, out, d, a.value, b.value);
     check_launch("binary_tiled");

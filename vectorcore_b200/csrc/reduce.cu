@@ -1635,7 +1635,7 @@ static void launch_expand_mode(const float* g, const long long* idx, const float
     unsigned* err = device_error_word();
     if (inner == 1) {
         const bool vec = length % 4 == 0 && aligned16(out);
-        const unsigned grid = static_cast<unsigned>(std::min<std::size_t>(outer, static_cast<std::size_t>(sm_count()) * 16));
+        const unsigned grid = static_cast<unsigned>(std::min<std::size_t>(outer, 0x7fffffffull));  // a CTA per row
         if (vec) expand_rows_kernel<MODE, true><<<grid, kThreads, 0, st>>>(g, idx, idxf, out, outer, length, err);
         else expand_rows_kernel<MODE, false><<<grid, kThreads, 0, st>>>(g, idx, idxf, out, outer, length, err);
     } else {
