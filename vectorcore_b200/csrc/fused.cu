@@ -39,11 +39,11 @@ constexpr unsigned kFwdThreads = 512;
 constexpr unsigned kFwdGroups = 8;
 constexpr unsigned long long kFwdPerCta = kFwdThreads * kFwdGroups;
 // backward, column strips: a CTA owns 16 floats of every row (four float4
-// lanes x 128 row slots, eight rows in flight per thread)
+// lanes x 128 row slots, six rows in flight per thread)
 constexpr unsigned kStripThreads = 512;
 constexpr unsigned kStripLanes = 4;
 constexpr unsigned kStripSlots = kStripThreads / kStripLanes;
-constexpr unsigned kStripRowsInFlight = 8;
+constexpr unsigned kStripRowsInFlight = 6;
 constexpr unsigned kStripCols = kStripLanes * 4;
 constexpr unsigned long long kStripMaxRows = 4096;
 
@@ -67,7 +67,9 @@ __device__ __forceinline__ bool arrive_last(unsigned* ticket, unsigned expected,
 // wave, and adds them in j order. The last CTA to arrive adds the per-CTA
 // partials in CTA order, each thread loading its partials before adding
 // (independent loads, one L2 round trip), then a fixed block tree.
-__global__ void __launch_bounds__(kFwdThreads)
+// Two CTAs per SM (at most 64 registers), so the 256 CTAs of a
+// 1024 x 4096 problem run in one wave on 148 SMs.
+__global__ void __launch_bounds__(kFwdThreads, 2)
 bias_relu_sum_fwd_wide(const float* __restrict__ x, const float* __restrict__ b, unsigned long long units,
                        FastDiv cols_fd, double* __restrict__ partial, unsigned* __restrict__ ticket,
                        float* __restrict__ loss, double* __restrict__ loss_d) {
@@ -76,23 +78,24 @@ bias_relu_sum_fwd_wide(const float* __restrict__ x, const float* __restrict__ b,
     pdl_wait();
     pdl_trigger();
     const unsigned long long base = static_cast<unsigned long long>(blockIdx.x) * kFwdPerCta;
-    float4 xv[kFwdGroups], bv[kFwdGroups];
+    float4 xv[kFwdGroups];
 #pragma unroll
     for (unsigned k = 0; k < kFwdGroups; ++k) {
         const unsigned long long e = base + k * kFwdThreads + threadIdx.x;
-        if (e < units) {
-            unsigned q, r;
-            cols_fd.divmod(static_cast<unsigned>(e), q, r);
-            xv[k] = ldg4(x + 4 * e);
-            bv[k] = ldg4(b + 4ull * r);
-        }
+        if (e < units) xv[k] = ldg4(x + 4 * e);
     }
+    // the bias groups (L1 hits: b is one row) are loaded as they are used,
+    // so the x groups alone hold registers while in flight
     double acc = 0.0;
 #pragma unroll
     for (unsigned k = 0; k < kFwdGroups; ++k) {
-        if (base + k * kFwdThreads + threadIdx.x >= units) continue;
-        const float y0 = relu_of(xv[k].x + bv[k].x), y1 = relu_of(xv[k].y + bv[k].y);
-        const float y2 = relu_of(xv[k].z + bv[k].z), y3 = relu_of(xv[k].w + bv[k].w);
+        const unsigned long long e = base + k * kFwdThreads + threadIdx.x;
+        if (e >= units) continue;
+        unsigned q, r;
+        cols_fd.divmod(static_cast<unsigned>(e), q, r);
+        const float4 bv = ldg4(b + 4ull * r);
+        const float y0 = relu_of(xv[k].x + bv.x), y1 = relu_of(xv[k].y + bv.y);
+        const float y2 = relu_of(xv[k].z + bv.z), y3 = relu_of(xv[k].w + bv.w);
         acc += static_cast<double>((y0 + y1) + (y2 + y3));
     }
     acc = block_sum(acc, s_red);
@@ -269,11 +272,11 @@ bias_relu_sum_bwd(const float* __restrict__ x, const float* __restrict__ b, cons
 // CTA k owns columns [16 k, 16 k + 16) of every row, so db needs no
 // cross-CTA step (no counter buffer, atomics or ticket). Thread (slot, lane)
 // = (tid / 4, tid % 4) owns the float4 column 16 k + 4 lane over rows
-// slot + 128 i: it loads eight rows together, writes dx and counts the rows
+// slot + 128 i: it loads six rows together, writes dx and counts the rows
 // with h > 0. A warp's eight slots meet by shuffles (lanes of one column are
 // 4 apart), the 16 warps through shared memory; integer counts are exact in
 // any order.
-__global__ void __launch_bounds__(kStripThreads)
+__global__ void __launch_bounds__(kStripThreads, 2)  // two CTAs per SM: 256 strips in one wave
 bias_relu_sum_bwd_strip(const float* __restrict__ x, const float* __restrict__ b, const float* __restrict__ upstream,
                         unsigned rows, unsigned long long cols, float* __restrict__ dx, float* __restrict__ db,
                         double* __restrict__ db_d) {
