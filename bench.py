@@ -539,7 +539,10 @@ def measure_e2e(args, sets, barrier, dist, torch, bytes_per_step, world, n):
         be.synchronize()
 
     loop(1)  # warm-up: copy streams, events, staging of the first tickets
-    steps = max(1, min(args.steps, 5))
+    # the pipeline fills with one step's upload and drains with one step's
+    # compute and download: time --steps steps (at most 20) so the steady
+    # state dominates, as in a long-running loader
+    steps = max(1, min(args.steps, 20))
     barrier()
     t0 = time.perf_counter()
     loop(steps)
