@@ -37,6 +37,56 @@ def test_binary_broadcast_bitexact(backend, port, a_shape, b_shape):
         assert_bitexact(got, port.binary(op, a, b), f"{name} {a_shape} {b_shape}")
 
 
+@pytest.mark.parametrize("n", [4095, 4096, 4097, 8191, 8196, (1 << 20) + 5, (3 << 20) + 2])
+def test_chunked_streams_across_chunk_ends(backend, port, n):
+    """The flat kernels give each CTA 4096 elements (1024 float4) and the
+    last CTA the n % 4 tail: sizes on both sides of chunk ends, forward and
+    backward, bit for bit (exp, log and sigmoid within 2 ulp)."""
+    rng = np.random.default_rng(n)
+    a = rng.uniform(0.1, 2, size=n).astype(np.float32)
+    b = rng.uniform(0.1, 2, size=n).astype(np.float32)
+    g = rng.uniform(-1, 1, size=n).astype(np.float32)
+    da_, db_, dg = dev(backend, a), dev(backend, b), dev(backend, g)
+    shape = (n,)
+    for name, op in OPS.items():
+        assert_bitexact(host(backend, backend.binary(da_, shape, None, db_, shape, None, shape, op), shape),
+                        port.binary(op, a, b), f"{name} n={n}")
+        ga, gb = backend.binary_backward(op, da_, shape, db_, shape, dg, shape)
+        ra, rb = port.binary_backward(op, a, b, g)
+        assert_bitexact(host(backend, ga, shape), ra, f"{name} da n={n}")
+        assert_bitexact(host(backend, gb, shape), rb, f"{name} db n={n}")
+    assert_bitexact(host(backend, backend.binary_scalar(da_, n, 0.5, B.MUL), shape),
+                    port.binary(B.MUL, a, np.array(0.5, np.float32)))
+    for op in (B.NEG, B.RELU, B.RELU_GRAD):
+        assert_bitexact(host(backend, backend.unary(dg, n, op), shape), port.unary(op, g), f"unary {op} n={n}")
+    for op, x, dx in ((B.SIGMOID, g, dg), (B.EXP, g, dg), (B.LOG, a, da_)):
+        assert_ulp(host(backend, backend.unary(dx, n, op), shape), port.unary(op, x), what=f"unary {op} n={n}")
+    assert_bitexact(host(backend, backend.unary_backward(B.RELU, dg, None, db_, n), shape),
+                    port.unary_backward(B.RELU, g, b), f"relu backward n={n}")
+    one = dev(backend, np.full(1, 0.25, np.float32))
+    got = host(backend, backend.broadcast_to(one, (1,), shape), shape)
+    assert (got == np.float32(0.25)).all()
+
+
+@pytest.mark.parametrize("lo,hi", [(-1.0, 1.0), (-20.0, 20.0), (-90.0, 90.0), (-110.0, 110.0)])
+def test_exp_log_sigmoid_wide_sweep(backend, port, lo, hi):
+    """2^22 inputs per range (log on |x| spread over 1e-38..1e38): the
+    table-driven float exp stays within 1 ulp of the reference's glibc
+    result, sigmoid and log within 2 -- including the inputs exp routes to
+    its double-precision fallback (|x| > 86, infinities, NaN)."""
+    rng = np.random.default_rng(int(hi))
+    x = rng.uniform(lo, hi, size=1 << 22).astype(np.float32)
+    x[:6] = [np.inf, -np.inf, np.nan, 0.0, -0.0, 86.0]
+    dx = dev(backend, x)
+    n = x.size
+    assert_ulp(host(backend, backend.unary(dx, n, B.EXP), x.shape), port.unary(B.EXP, x), max_ulp=1, what="exp")
+    assert_ulp(host(backend, backend.unary(dx, n, B.SIGMOID), x.shape), port.unary(B.SIGMOID, x), what="sigmoid")
+    lx = np.exp(rng.uniform(np.log(1e-38), np.log(1e38), size=1 << 22)).astype(np.float32)
+    lx[:5] = [np.inf, 0.0, 1e-40, 1.0, np.float32(0.75)]
+    assert_ulp(host(backend, backend.unary(dev(backend, lx), n, B.LOG), lx.shape), port.unary(B.LOG, lx),
+               what="log")
+
+
 @pytest.mark.parametrize("shape", [(1,), (3,), (127,), (1023,), (4097,), (65537,), (2, 3, 5, 7), ()])
 def test_binary_odd_sizes_and_rank0(backend, port, shape):
     rng = np.random.default_rng(sum(shape) + 1)

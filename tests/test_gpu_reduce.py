@@ -26,8 +26,10 @@ def split(shape, axis):
             int(np.prod(shape[ax + 1:], dtype=np.int64)))
 
 
-@pytest.mark.parametrize("n", [1, 3, 127, 1024, 65535, 65536, 65537, 3_000_001])
+@pytest.mark.parametrize("n", [1, 3, 127, 1024, 65535, 65536, 65537, 3_000_001, (1 << 24) + 7, 1 << 26])
 def test_reduce_all(backend, port, n):
+    # past 2^24 elements the full reductions take >= 1024 segments of 16384
+    # and finish with 1024 threads per output
     x = np.random.default_rng(n).normal(size=n).astype(np.float32)
     dx = dev(backend, x)
     got = backend.download(backend.reduce_sum(dx, n))[0]

@@ -35,6 +35,76 @@ __device__ __forceinline__ float bop(float x, float y) {
     else return x / y;
 }
 
+// exp rounded once from double precision: CUDA's double exp is within 1 ulp
+// of a double, so the rounding to float is correct except within about 2^-29
+// of a rounding boundary. Only for the inputs exp_acc leaves aside; kept out
+// of line so the unrolled stream loops carry one call, not sixteen copies.
+__device__ __noinline__ float exp_rn(float x) { return static_cast<float>(exp(static_cast<double>(x))); }
+
+// Why exp_acc: glibc's float exp (the reference's std::exp on float) is
+// within 0.502 ulp of the true value and CUDA's expf within 2 ulp, so the two
+// can land 3 floats apart; a 16 M-sample sweep found sigmoid inputs 3 ulp from
+// the reference, outside the 2-ulp class. Double exp closes the gap but costs
+// 25-40% of the stream's speed; exp_acc stays within ~0.52 ulp of the true
+// value (at most one float from glibc's) at close to expf's cost. log keeps
+// CUDA's logf: the same sweep found it within 1 ulp of glibc's logf.
+
+// Rounding to an integer by adding 1.5 * 2^23 (exact for |v| < 2^22): the
+// float and integer forms of rint(v) come from FMA-pipe adds and an integer
+// subtract instead of conversion instructions, which issue at a quarter of
+// the rate on the SM.
+constexpr float kRoundMagic = 0x1.8p+23f;
+constexpr int kRoundMagicBits = 0x4b400000;
+
+// e^x, Tang's table-driven method (ACM TOMS 15(2), 1989) with a 32-entry
+// table. n = 32 m + j = rint(x * 32 / ln 2), r = x - n * ln2/32 from a
+// two-part ln2/32 (the first product exact inside an FMA), |r| <= ln2/64;
+// e^x = 2^m * 2^(j/32) * e^r with 2^(j/32) = T_hi + T_lo (float pair) and
+// e^r - 1 = r + r^2 (1/2 + r/6 + r^2/24) (truncation 2^-39). Every term but
+// T_hi is below 0.022 in magnitude, so their rounding errors stay near 0.01
+// ulp of the result and the last addition T_hi + s rounds once: ~0.52 ulp.
+// |x| > 86 (results near or below FLT_MIN, overflow), infinities and NaN
+// take exp_rn. Table: 2^(j/32) rounded to float and the remainder, computed
+// to 60 digits; constants 32 / ln 2, ln2/32 rounded to float and its
+// remainder.
+__device__ const float2 kExp2Frac[32] = {
+    {0x1p+0f, 0x0p+0f},                       {0x1.059b0ep+0f, -0x1.9d4f52p-25f},
+    {0x1.0b5586p+0f, 0x1.9f3122p-25f},        {0x1.11301ep+0f, -0x1.fdb496p-25f},
+    {0x1.172b84p+0f, -0x1.c15742p-27f},       {0x1.1d4874p+0f, -0x1.d2e8cap-25f},
+    {0x1.2387a6p+0f, 0x1.ceac48p-25f},        {0x1.29e9e0p+0f, -0x1.5c0424p-25f},
+    {0x1.306fe0p+0f, 0x1.4636e2p-25f},        {0x1.371a74p+0f, -0x1.18aac6p-25f},
+    {0x1.3dea64p+0f, 0x1.824684p-25f},        {0x1.44e086p+0f, 0x1.8624b4p-30f},
+    {0x1.4bfdaep+0f, -0x1.593abcp-25f},       {0x1.5342b6p+0f, -0x1.2c5610p-25f},
+    {0x1.5ab07ep+0f, -0x1.5bd5ecp-27f},       {0x1.6247ecp+0f, -0x1.f8b550p-25f},
+    {0x1.6a09e6p+0f, 0x1.9fcef4p-26f},        {0x1.71f75ep+0f, 0x1.1d8beep-25f},
+    {0x1.7a1148p+0f, -0x1.829fd0p-25f},       {0x1.82589ap+0f, -0x1.accc7cp-26f},
+    {0x1.8ace54p+0f, 0x1.15506ep-27f},        {0x1.93737cp+0f, -0x1.e64744p-25f},
+    {0x1.9c4918p+0f, 0x1.51f848p-27f},        {0x1.a5503cp+0f, -0x1.b83b54p-25f},
+    {0x1.ae89fap+0f, -0x1.a94b14p-26f},       {0x1.b7f770p+0f, -0x1.a09438p-25f},
+    {0x1.c199bep+0f, -0x1.3d56b2p-27f},       {0x1.cb720ep+0f, -0x1.8837ccp-27f},
+    {0x1.d5818ep+0f, -0x1.822dbcp-27f},       {0x1.dfc974p+0f, -0x1.908c94p-25f},
+    {0x1.ea4afap+0f, 0x1.52486cp-27f},        {0x1.f50766p+0f, -0x1.246eb0p-26f},
+};
+constexpr float kInvLn2x32 = 0x1.715476p+5f;
+constexpr float kLn2d32Hi = 0x1.62e430p-6f;
+constexpr float kLn2d32Lo = -0x1.05c610p-34f;
+
+__device__ __forceinline__ float exp_acc(float x) {
+    if (!(fabsf(x) <= 86.0f)) return exp_rn(x);
+    const float tm = fmaf(x, kInvLn2x32, kRoundMagic);  // |x * 32 / ln 2| < 2^12
+    const int n = __float_as_int(tm) - kRoundMagicBits;
+    const float nf = tm - kRoundMagic;
+    const float r1 = fmaf(-nf, kLn2d32Hi, x);
+    const float r2 = -nf * kLn2d32Lo;
+    const float poly = fmaf(r1, fmaf(r1, 1.0f / 24.0f, 1.0f / 6.0f), 0.5f);
+    const float q = fmaf(r1 * r1, poly, r2);
+    const float2 t = __ldg(&kExp2Frac[n & 31]);
+    float s = fmaf(t.x, q, t.y);
+    s = fmaf(t.x, r1, s);
+    const float y = t.x + s;
+    return __int_as_float(__float_as_int(y) + ((n >> 5) << 23));
+}
+
 template <int OP>
 __device__ __forceinline__ float uop(float x) {
     if constexpr (OP == VC_NEG) return -x;
@@ -44,12 +114,12 @@ __device__ __forceinline__ float uop(float x) {
         // cpu_backend.cpp:302-307 computes 1/(1+exp(-x)) for x >= 0 and
         // e/(1+e) with e = exp(x) otherwise. Both branches evaluate
         // exp(-|x|), so selecting the numerator gives the same bits with one
-        // expf and one division and no warp divergence (NaN takes the second
-        // form, as in the reference).
-        const float e = expf(-fabsf(x));
+        // exponential and one division and no warp divergence (NaN takes the
+        // second form, as in the reference).
+        const float e = exp_acc(-fabsf(x));
         const float num = x >= 0.0f ? 1.0f : e;
         return num / (1.0f + e);
-    } else if constexpr (OP == VC_EXP) return expf(x);
+    } else if constexpr (OP == VC_EXP) return exp_acc(x);
     else return logf(x);
 }
 
