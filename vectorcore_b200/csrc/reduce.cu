@@ -1774,16 +1774,25 @@ vc_status vc_cuda_binary_backward(int op, const float* a, const size_t* a_shape,
     if (da && db && try_fused_bcast_backward(op, a, sa, b, sb, g, sg, src, rank, da, db, nullptr, nullptr,
                                              checked_numel(b_shape, b_rank)))
         return VC_OK;
-    if (da) {
-        Src ops[3] = {sg, sb, sb};
-        const int f = (op == VC_ADD || op == VC_SUB) ? V_G : (op == VC_MUL ? V_MUL : V_DIV_A);
-        vjp_reduce(f, ops, src, rank, a_shape, a_rank, da);
+    // The two gradients are independent reductions: with both wanted, db's
+    // runs on the side stream while da's runs on the main one, so their
+    // small latency-bound launches (compact sums, finishes) hide under each
+    // other's streams -- e.g. sum()'s scalar upstream on a [P,1,R,L] x
+    // [1,Q,1,L] product writes da and reads a at the same time.
+    const int fa = (op == VC_ADD || op == VC_SUB) ? V_G : (op == VC_MUL ? V_MUL : V_DIV_A);
+    const int fb = op == VC_ADD ? V_G : (op == VC_SUB ? V_NEG : (op == VC_MUL ? V_MUL : V_DIV_B));
+    Src ops_a[3] = {sg, sb, sb};
+    Src ops_b[3] = {sg, sa, sb};
+    if (da && db) {
+        SideStream side;
+        vjp_reduce(fb, ops_b, src, rank, b_shape, b_rank, db);
+        side.leave();
+        vjp_reduce(fa, ops_a, src, rank, a_shape, a_rank, da);
+        side.join();
+        return VC_OK;
     }
-    if (db) {
-        Src ops[3] = {sg, sa, sb};
-        const int f = op == VC_ADD ? V_G : (op == VC_SUB ? V_NEG : (op == VC_MUL ? V_MUL : V_DIV_B));
-        vjp_reduce(f, ops, src, rank, b_shape, b_rank, db);
-    }
+    if (da) vjp_reduce(fa, ops_a, src, rank, a_shape, a_rank, da);
+    if (db) vjp_reduce(fb, ops_b, src, rank, b_shape, b_rank, db);
     VC_API_END
 }
 

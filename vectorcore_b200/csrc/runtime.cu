@@ -155,6 +155,7 @@ struct State {
     int sms{148};
     cudaStream_t own_stream{nullptr};
     cudaStream_t stream{nullptr};
+    cudaStream_t side{nullptr};  // second compute stream (SideStream), created on first use
     unsigned* counters{nullptr};
     unsigned* error_word{nullptr};
     char name[256]{};
@@ -259,7 +260,14 @@ void ensure_init() {
     if (cudaGetDevice(&current) == cudaSuccess && current != state().device) VC_CUDA(cudaSetDevice(state().device));
 }
 
-cudaStream_t stream() { return state().stream; }
+namespace {
+// Work issued by this host thread inside a SideStream goes to the side
+// stream, and the scratch it frees waits for the join.
+thread_local cudaStream_t t_stream_override = nullptr;
+thread_local std::vector<void*>* t_deferred_frees = nullptr;
+}  // namespace
+
+cudaStream_t stream() { return t_stream_override ? t_stream_override : state().stream; }
 int sm_count() { return state().sms; }
 unsigned* counters() { return state().counters; }
 unsigned* device_error_word() { return state().error_word; }
@@ -366,7 +374,53 @@ static void pool_free(void* p) {
 Scratch::Scratch(std::size_t bytes) : ptr_(pool_alloc(bytes)) {}
 Scratch::~Scratch() {
     try {
-        pool_free(ptr_);
+        if (t_deferred_frees && ptr_) t_deferred_frees->push_back(ptr_);
+        else pool_free(ptr_);
+    } catch (...) {
+    }
+}
+
+SideStream::SideStream() {
+    State& s = state();
+    {
+        std::lock_guard<std::mutex> lock(s.init_mutex);
+        if (!s.side) VC_CUDA(cudaStreamCreateWithFlags(&s.side, cudaStreamNonBlocking));
+    }
+    static thread_local cudaEvent_t events[2] = {nullptr, nullptr};
+    for (auto& e : events)
+        if (!e) VC_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    fork_ = events[0];
+    join_ = events[1];
+    main_ = s.stream;
+    side_ = s.side;
+    VC_CUDA(cudaEventRecord(fork_, main_));
+    VC_CUDA(cudaStreamWaitEvent(side_, fork_, 0));
+    t_stream_override = side_;
+    t_deferred_frees = &deferred_;
+    active_ = true;
+}
+
+void SideStream::leave() {
+    if (!active_) return;
+    t_stream_override = nullptr;
+    t_deferred_frees = nullptr;
+    active_ = false;
+}
+
+void SideStream::join() {
+    leave();
+    if (joined_) return;
+    joined_ = true;
+    VC_CUDA(cudaEventRecord(join_, side_));
+    VC_CUDA(cudaStreamWaitEvent(main_, join_, 0));
+    // the main stream now runs after the side work: its scratch may be reused
+    for (void* p : deferred_) pool_free(p);
+    deferred_.clear();
+}
+
+SideStream::~SideStream() {
+    try {
+        join();
     } catch (...) {
     }
 }

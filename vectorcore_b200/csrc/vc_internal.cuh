@@ -10,6 +10,7 @@
 #include <cstdint>
 #include <stdexcept>
 #include <string>
+#include <vector>
 
 namespace vc {
 
@@ -74,6 +75,30 @@ public:
     template <typename T> T* as() const { return static_cast<T*>(ptr_); }
 private:
     void* ptr_{nullptr};
+};
+
+// Fork / join of a second compute stream for two independent halves of one
+// call (e.g. the two gradients of a broadcast binary op): the constructor
+// makes the side stream wait for the work enqueued so far and routes this
+// host thread's launches to it; leave() routes them back to the main stream;
+// join() (also on destruction) makes the main stream wait for the side work.
+// Scratch the side work frees is returned to the pool only after the join,
+// so nothing on the main stream can be handed a block still in use there.
+// Enqueue the side half first: its allocations then precede the main half's
+// frees, so it cannot be handed a block the main half still uses.
+class SideStream {
+public:
+    SideStream();
+    ~SideStream();
+    SideStream(const SideStream&) = delete;
+    SideStream& operator=(const SideStream&) = delete;
+    void leave();
+    void join();
+private:
+    cudaStream_t main_{nullptr}, side_{nullptr};
+    cudaEvent_t fork_{nullptr}, join_{nullptr};
+    std::vector<void*> deferred_;
+    bool active_{false}, joined_{false};
 };
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<std::uintptr_t>(p) & 15u) == 0; }
