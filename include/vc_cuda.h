@@ -14,7 +14,11 @@
  *    (the reference's Shape / Strides = std::vector<std::size_t>,
  *    include/vectorcore/shape.hpp:9-10).
  *  - All work is enqueued on one CUDA stream per process (vc_cuda_stream());
- *    calls return before the GPU finishes. Only vc_cuda_download() and
+ *    calls return before the GPU finishes. A call with two independent
+ *    halves (the two gradients of vc_cuda_binary_backward) may run one half
+ *    on an internal second stream, forked from and joined back to that
+ *    stream with events before it returns, so work ordered on
+ *    vc_cuda_stream() sees the whole result. Only vc_cuda_download() and
  *    vc_cuda_synchronize() block, as MetalBackend::download / synchronize do
  *    (src/metal/metal_backend.mm:205-211, 415-444).
  *  - Errors detected on the device (bounded waits that gave up, out-of-range
