@@ -1008,6 +1008,16 @@ static std::size_t fused_smem(unsigned US) {
 // reduce-scatter in the fixed tree ((r0 + r1) + (r2 + r3)) per component,
 // three shuffles instead of eight. Lane row slot k ends with component
 // (k & 1) * 2 + (k >> 1) of the column.
+// Read-only float4 load that asks L2 to fetch the whole 256-byte block around
+// it: the fused backward reads g in 128-byte pieces (32 floats of a row per
+// CTA) and the CTA on the neighbouring 32 floats runs at the same time, so
+// each DRAM access serves both (dense-g backward of configuration 5: about
+// one point of HBM bandwidth, 84-85% -> 86%).
+__device__ __forceinline__ float4 ld4_l2_256(const float* p) {
+    float4 v;
+    asm("ld.global.nc.L2::256B.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+    return v;
+}
 __device__ __forceinline__ float fold4_scatter(float4 v, unsigned k) {
     const bool odd = k & 1u, high = k & 2u;
     float keep0 = odd ? v.z : v.x, keep1 = odd ? v.w : v.y;
@@ -1106,7 +1116,7 @@ bcast_backward_fused(const float* __restrict__ g, const float* __restrict__ a, c
             const long long go = static_cast<long long>(c0) * d.gu0 + static_cast<long long>(c1) * d.gu1;
 #pragma unroll
             for (unsigned i = 0; i < NV; ++i)
-                gv[k][i] = sok[k] && vok[i] ? ld4_stream(gp[i] + go) : make_float4(0.f, 0.f, 0.f, 0.f);
+                gv[k][i] = sok[k] && vok[i] ? ld4_l2_256(gp[i] + go) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
         float* pb = part + (n & 1u) * UNR * kFWarps * 32;
         const float4* ab = arow + (n & 1u) * UNR * d.US * kFCols;
