@@ -28,7 +28,7 @@ namespace {
 constexpr unsigned kThreads = 256;
 // Aim for about this many threads of work before splitting a reduction into
 // segments (a constant, so the split depends on the problem size alone).
-constexpr unsigned long long kTargetThreads = 1ull << 19;
+constexpr unsigned long long kTargetThreads = 1ull << 17;  // 2^19 split axis-0 reductions 4x finer: partials and finishes cost 2.5 points
 constexpr unsigned long long kMinSegment = 16;         // reduced positions per segment (column)
 // Column sums take at most this many segments, so the partials stay small
 // next to the input when the outputs are few (the compact reductions of a
