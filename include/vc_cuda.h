@@ -390,14 +390,18 @@ vc_status vc_cuda_transpose_last2(const float* in, float* out, size_t batch, siz
 
 /* ---- allocation-free sum ---------------------------------------------------- */
 
-/* out[0] = sum of the `count` floats at `in` (device memory), the same value
- * vc_cuda_reduce_all(VC_REDUCE_SUM, ...) computes (double accumulation, one
- * rounding), for callers that must not allocate device memory: hosts that
- * reserved the device's memory up front under a hard budget, or loops that
- * cannot stall on cudaMalloc / cudaFree. No counterpart in the reference.
+/* out[0] = sum of the `count` floats at `in` (device memory): double
+ * accumulation in 65536-element chunks, rounded once, so it agrees with
+ * vc_cuda_reduce_all(VC_REDUCE_SUM, ...) within double-accumulation rounding
+ * (the two split the input differently). For callers that must not allocate
+ * device memory: hosts that reserved the device's memory up front under a
+ * hard budget, or loops that cannot stall on cudaMalloc / cudaFree. No
+ * counterpart in the reference.
  *  - Allocates nothing: its scratch (4096 doubles, 32 KiB) is an array
  *    compiled into this library, held by every GPU that loads it until the
- *    process exits. Call vc_cuda_init first (it creates the stream).
+ *    process exits. Call vc_cuda_init first (it creates the stream); any
+ *    host thread may then call it -- the call binds the thread to the
+ *    library's GPU, as every other entry point does.
  *  - count <= 268435456 (2^28, one partial per 65536 elements); larger
  *    counts fail with VC_ERR_OVERFLOW before anything is launched.
  *  - The first call on a device looks up the array's device address

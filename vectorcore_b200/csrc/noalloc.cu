@@ -68,8 +68,8 @@ noalloc_finish(const double* __restrict__ partials, unsigned chunks, float* __re
 std::mutex g_mutex;
 double* g_address[kMaxDevices] = {};
 
-// Device address of the array on the current device, looked up once per
-// device (with that device current) and cached.
+// Device address of the array on `device`, looked up once per device and
+// cached. The caller has made `device` current on this thread.
 double* partials_address(int device) {
     if (device < 0 || device >= kMaxDevices) fail(VC_ERR_RUNTIME, "device index out of range for the allocation-free sum");
     std::lock_guard<std::mutex> lock(g_mutex);
@@ -95,12 +95,14 @@ extern "C" {
 
 vc_status vc_cuda_reduce_sum_noalloc(const float* in, size_t count, float* out) {
     VC_API_BEGIN
-    int device = -1;
-    if (cudaGetDevice(&device) != cudaSuccess || !stream()) {
-        cudaGetLastError();
+    if (!initialized())
         fail(VC_ERR_RUNTIME, "vc_cuda_reduce_sum_noalloc: call vc_cuda_init first (this entry point allocates "
                              "nothing, not even the device's stream)");
-    }
+    // The calling host thread may never have called into the library, or may
+    // have another GPU current: bind it to the library's GPU, whose stream
+    // the kernels go to and whose copy of the array they must use.
+    ensure_init();
+    const int device = bound_device();
     if (!out) fail(VC_ERR_INVALID, "vc_cuda_reduce_sum_noalloc: null output");
     if (count > kMaxCount)
         fail(VC_ERR_OVERFLOW, "vc_cuda_reduce_sum_noalloc: " + std::to_string(count) +

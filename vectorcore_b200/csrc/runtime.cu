@@ -260,6 +260,9 @@ void ensure_init() {
     if (cudaGetDevice(&current) == cudaSuccess && current != state().device) VC_CUDA(cudaSetDevice(state().device));
 }
 
+bool initialized() { return state().ready; }
+int bound_device() { return state().ready ? state().device : -1; }
+
 namespace {
 // Work issued by this host thread inside a SideStream goes to the side
 // stream, and the scratch it frees waits for the join.

@@ -51,6 +51,8 @@ void check_cuda(cudaError_t err, const char* what);
 // Runtime state (runtime.cu).
 // ---------------------------------------------------------------------------
 void ensure_init();              // init device 0 if nothing was selected yet
+bool initialized();              // vc_cuda_init (or a first call) has bound a GPU
+int bound_device();              // that GPU's index (-1 before initialisation)
 cudaStream_t stream();           // the enqueue stream
 int sm_count();
 unsigned* counters();            // zeroed ticket counters (kCounterSlots)
