@@ -378,14 +378,27 @@ def reference() -> Reference:
     return _ref
 
 
+def _configured_reference() -> str:
+    """The reference checkout named by the repository's BASELINE.json
+    (``reference_path``), used when VECTORCORE_REF is not set."""
+    import json
+
+    try:
+        return str(json.loads((HERE.parent / "BASELINE.json").read_text()).get("reference_path") or "")
+    except (OSError, ValueError):
+        return ""
+
+
 def build(quiet: bool = True) -> None:
-    """Compile the restatement and, when the reference checkout is present,
-    the reference's own CPU path (``make -C oracle``)."""
+    """Compile the restatement and, when the reference checkout is present
+    (VECTORCORE_REF, else BASELINE.json's reference_path), the reference's
+    own CPU path, its device-slot build and its build with the cuda device
+    (``make -C oracle``)."""
     import subprocess
 
-    ref = os.environ.get("VECTORCORE_REF", "/root/reference")
-    # "slot" links the reference's sources to the CUDA library, so it needs
-    # vectorcore_b200/_lib/libvc_cuda.so to be built first.
-    targets = ["oracle"] + (["ref", "slot"] if Path(ref, "src").is_dir() else [])
+    ref = os.environ.get("VECTORCORE_REF") or _configured_reference()
+    # "slot" and "host" link the reference's sources to the CUDA library, so
+    # they need vectorcore_b200/_lib/libvc_cuda.so to be built first.
+    targets = ["oracle"] + (["ref", "slot", "host"] if ref and Path(ref, "src").is_dir() else [])
     subprocess.run(["make", "-s", "-C", str(HERE), f"REF={ref}", *targets], check=True,
                    stdout=subprocess.DEVNULL if quiet else None)

@@ -5,7 +5,7 @@ from __future__ import annotations
 
 import math
 
-from .backend import CudaBackend
+from vectorcore_b200.backend import CudaBackend
 from .tensor import NoGradGuard, Tensor, cross_entropy  # noqa: F401
 
 

@@ -1,4 +1,9 @@
-"""Tensor and reverse-mode autograd for the cuda device.
+"""Tensor and reverse-mode autograd over the C ABI -- a TEST HELPER.
+
+The reference itself runs on the cuda device through its own host
+(reference_cuda_device.patch, exercised by tests/test_gpu_reference_host.py).
+This Python restatement of its Tensor layer lets tests drive the fused entry
+points and CUDA graphs through a Tensor-shaped API without a C++ build.
 
 Mirrors the reference's public Tensor API (include/vectorcore/tensor.hpp,
 python/bindings.cpp:63-179) -- same names, argument meaning, shapes, error
@@ -19,8 +24,8 @@ from typing import Optional, Sequence
 
 import numpy as np
 
-from . import backend as _B
-from .backend import CudaBackend, CudaStorage
+from vectorcore_b200 import backend as _B
+from vectorcore_b200.backend import CudaBackend, CudaStorage
 
 _state = threading.local()
 

@@ -15,7 +15,7 @@ import pytest
 
 import _cases as C
 import oracle
-import vectorcore_b200 as vc
+import pytensor as vc
 from _util import assert_bitexact, assert_sum_close, sha256
 
 pytestmark = pytest.mark.gpu

@@ -127,7 +127,7 @@ def test_pageable_copies_through_staging(backend, elements):
 
 
 def test_tensor_to_round_trip_large(backend):
-    import vectorcore_b200 as vc
+    import pytensor as vc
 
     x = np.random.default_rng(5).normal(size=(3000, 7001)).astype(np.float32)
     t = vc.Tensor(x, requires_grad=True)

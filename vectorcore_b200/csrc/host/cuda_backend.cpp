@@ -6,13 +6,15 @@
 #include <stdexcept>
 #include <string>
 
-// The Device value CUDA storages report. A host with a DeviceType::CUDA
-// enumerator compiles this file with
-//   -DVECTORCORE_CUDA_DEVICE='::vectorcore::Device(::vectorcore::DeviceType::CUDA)'.
-// The plugin-slot build (metal_slot.cpp) serves the reference's existing
-// non-CPU device value.
+// The Device value CUDA storages report: Device::cuda() on a host whose
+// device.hpp has the CUDA enumerator; the plugin-slot build (metal_slot.cpp)
+// serves the reference's existing non-CPU device value instead.
 #ifndef VECTORCORE_CUDA_DEVICE
+#ifdef VECTORCORE_HAS_CUDA_DEVICE
+#define VECTORCORE_CUDA_DEVICE ::vectorcore::Device::cuda()
+#else
 #define VECTORCORE_CUDA_DEVICE ::vectorcore::Device::metal()
+#endif
 #endif
 
 namespace vectorcore {
@@ -157,6 +159,34 @@ void CudaBackend::axpy_inplace(Storage& target, const Storage& source, std::size
 
 void CudaBackend::synchronize() { check(vc_cuda_synchronize(), "synchronize failed"); }
 
+std::shared_ptr<Storage> CudaBackend::broadcast_to(const Storage& value, const Shape& value_shape,
+                                                   const Shape& target_shape) {
+    auto out = make(count_of(target_shape), device_);
+    check(vc_cuda_broadcast_to(ptr(value), value_shape.data(), static_cast<int>(value_shape.size()),
+                               out->device_data(), target_shape.data(), static_cast<int>(target_shape.size())),
+          "broadcast_to failed");
+    return out;
+}
+
+CudaBackend::MaxResult CudaBackend::max_with_index(const Storage& input, std::size_t outer, std::size_t length,
+                                                   std::size_t inner) {
+    MaxResult r{make(outer * inner, device_), make(outer * inner, device_, sizeof(std::int64_t))};
+    check(vc_cuda_reduce_axis(VC_REDUCE_MAX, ptr(input), outer, length, inner, ptr(*r.values),
+                              static_cast<int64_t*>(as_cuda(*r.indices).raw())),
+          "max failed");
+    return r;
+}
+
+std::shared_ptr<Storage> CudaBackend::max_backward(const Storage& gradient, const Storage& indices, std::size_t outer,
+                                                   std::size_t length, std::size_t inner) {
+    auto out = make(outer * length * inner, device_);
+    check(vc_cuda_reduce_axis_backward(VC_REDUCE_MAX, ptr(gradient),
+                                       static_cast<const int64_t*>(as_cuda(indices).raw()), out->device_data(), outer,
+                                       length, inner),
+          "max backward failed");
+    return out;
+}
+
 std::shared_ptr<Storage> CudaBackend::sum_to_shape(const Storage& gradient, const Shape& g_shape,
                                                    const Shape& target_shape) {
     auto out = make(count_of(target_shape), device_);
@@ -238,6 +268,14 @@ std::shared_ptr<Storage> CudaBackend::cross_entropy_backward(const Storage& logi
                                          batch, out->device_data()),
           "cross_entropy_backward failed");
     return out;
+}
+
+bool cuda_available() { return CudaBackend::instance().available(); }
+
+std::string cuda_device_name() { return CudaBackend::instance().device_name(); }
+
+void cuda_synchronize() {
+    if (CudaBackend::instance().available()) CudaBackend::instance().synchronize();
 }
 
 }  // namespace vectorcore

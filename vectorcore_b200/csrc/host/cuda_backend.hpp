@@ -5,9 +5,12 @@
 // CudaBackend has that method set, with the same argument meaning, on top of
 // the C ABI in include/vc_cuda.h, plus the fused entry points of the CUDA
 // device. It compiles against the reference's own headers (Storage, Shape,
-// cpu::BinaryOp/UnaryOp/ReduceOp): a maintainer adds this file and
-// cuda_backend.cpp under src/cuda/ and routes a `cuda` Device to
-// CudaBackend::instance() at the dispatch sites.
+// cpu::BinaryOp/UnaryOp/ReduceOp): the host gains a DeviceType::CUDA and
+// routes it to CudaBackend::instance() at its dispatch sites
+// (src/ops.cpp:31-39 and the others), as reference_cuda_device.patch in this
+// directory does. Storages report Device::cuda() when the host's device.hpp
+// defines VECTORCORE_HAS_CUDA_DEVICE, else the host's non-CPU device value
+// (the plugin-slot build, metal_slot.cpp).
 //
 // Errors: every failing vc_cuda_* call becomes the reference's exception type
 // for the status -- std::invalid_argument, std::out_of_range,
@@ -83,6 +86,22 @@ public:
     void synchronize();
 
     // ---- fused entry points of the CUDA device ------------------------------
+    // detail::broadcast_to (src/autograd.cpp:74-91): value + 0 into target_shape,
+    // without the one-float upload of the scalar zero the reference adds.
+    [[nodiscard]] std::shared_ptr<Storage> broadcast_to(const Storage& value, const Shape& value_shape,
+                                                        const Shape& target_shape);
+    // max along the middle axis together with its first-maximum index (int64),
+    // one pass; the reference runs a second argmax pass when grad is needed
+    // (src/ops.cpp:323-331).
+    struct MaxResult {
+        std::shared_ptr<Storage> values, indices;
+    };
+    [[nodiscard]] MaxResult max_with_index(const Storage& input, std::size_t outer, std::size_t length,
+                                           std::size_t inner);
+    // The max backward: the upstream gradient scattered at the int64 indices
+    // (cpu::scatter_axis, src/cpu/cpu_backend.cpp:462-471).
+    [[nodiscard]] std::shared_ptr<Storage> max_backward(const Storage& gradient, const Storage& indices,
+                                                        std::size_t outer, std::size_t length, std::size_t inner);
     // detail::sum_to_shape (src/autograd.cpp:50-72) in one strided reduce.
     [[nodiscard]] std::shared_ptr<Storage> sum_to_shape(const Storage& gradient, const Shape& g_shape,
                                                         const Shape& target_shape);
@@ -117,5 +136,13 @@ public:
 private:
     Device device_;
 };
+
+// Free functions next to metal_available() / metal_device_name() /
+// synchronize() (include/vectorcore/metal_backend.hpp:58-63).
+[[nodiscard]] bool cuda_available();
+[[nodiscard]] std::string cuda_device_name();
+// Block until the CUDA device's queued work finished and surface its
+// asynchronous errors; a no-op when no CUDA device is usable.
+void cuda_synchronize();
 
 }  // namespace vectorcore

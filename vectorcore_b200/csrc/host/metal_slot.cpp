@@ -4,14 +4,15 @@
 // interface: src/metal/metal_backend.mm on Apple, src/metal/
 // metal_backend_stub.cpp elsewhere (include/vectorcore/metal_backend.hpp:13-63).
 // Its dispatch sites send every non-CPU tensor to MetalBackend::instance()
-// (src/ops.cpp:31-39 and the other sites listed in INTEGRATION.md). This file
+// (src/ops.cpp:31-39, src/autograd.cpp:81-89, src/tensor.cpp:57-64, ...). This file
 // is a third implementation of that interface which forwards to CudaBackend:
 // linked with the reference's UNMODIFIED sources in place of the stub, the
 // reference's own Tensor / autograd / nn / pybind11 surface runs on the B200,
 // with the non-CPU device value (spelled "metal" by the reference's
 // Device::str()) meaning the CUDA device. It demonstrates the drop-in
-// boundary without editing a reference file; a maintainer's integration adds
-// DeviceType::CUDA and calls CudaBackend directly.
+// boundary without editing a reference file; the integration proper adds
+// DeviceType::CUDA next to CPU and Metal and calls CudaBackend directly
+// (reference_cuda_device.patch in this directory).
 #include "cuda_backend.hpp"
 
 #include "vectorcore/metal_backend.hpp"

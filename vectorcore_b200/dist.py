@@ -14,6 +14,12 @@ cross-entropy stay local.
 ``Communicator.from_torch()`` bootstraps the NCCL communicator through an
 initialised ``torch.distributed`` process group (any backend -- the 128-byte
 id is all that travels over it).
+
+The functions work at the device-plugin level (``CudaStorage`` + shapes, like
+``backend.CudaBackend``): each returns the combined result, identical on
+every rank, and the backward of a sharded reduction needs no communication
+(the upstream gradient is broadcast over the rank's own rows). Every rank
+must make the same calls in the same order: each is a collective.
 """
 from __future__ import annotations
 
@@ -25,7 +31,6 @@ import numpy as np
 from . import _abi
 from . import backend as _B
 from .backend import CudaBackend, CudaStorage
-from .tensor import Tensor, _attach, _out, _require_cuda
 
 UNIQUE_ID_BYTES = 128
 
@@ -114,8 +119,9 @@ def _p(s):
     return None if s is None else ctypes.c_void_p(s.ptr)
 
 
-def _sum_over_shards(comm: Communicator, partial: CudaStorage, count: int, divisor: float = 0.0,
-                     negate: bool = False) -> CudaStorage:
+def _combine_sums(comm: Communicator, partial: CudaStorage, count: int, divisor: float = 0.0,
+                  negate: bool = False) -> CudaStorage:
+    """All-gather `count` double partials per rank and add them in rank order."""
     gathered = comm.allgather(partial, count * 8, np.float64)
     out = CudaStorage(count)
     _abi.call("vc_cuda_combine_partials", _B.REDUCE_SUM, _p(gathered), None, None, comm.world,
@@ -123,101 +129,109 @@ def _sum_over_shards(comm: Communicator, partial: CudaStorage, count: int, divis
     return out
 
 
-def sum_axis0(x: Tensor, comm: Communicator, mean_rows: int = 0) -> Tensor:
-    """Sum (or mean over `mean_rows` global rows) of the row-sharded `x` over
-    its leading axis; the same result on every rank. Backward: the upstream
-    gradient broadcast to this rank's rows (no communication)."""
-    _require_cuda(x)
-    be = _be()
-    shape = x._impl.shape
-    rows_local, rest = shape[0], tuple(shape[1:])
-    count = int(np.prod(rest, dtype=np.int64))
+def sum_axis0(x: CudaStorage, rows_local: int, count: int, comm: Communicator, mean_rows: int = 0) -> CudaStorage:
+    """Sum (or the mean over `mean_rows` global rows) over the sharded leading
+    axis of x [rows_local, count]: [count] floats, the same on every rank.
+    The backward is local: ``sum_axis0_backward``."""
     partial = CudaStorage(count, np.float64)
-    _abi.call("vc_cuda_reduce_axis_partial", _B.REDUCE_SUM, _p(x._impl.storage), ctypes.c_size_t(1),
-              ctypes.c_size_t(rows_local), ctypes.c_size_t(count), ctypes.c_int64(0), 0, _p(partial), None, None)
-    out = _out(_sum_over_shards(comm, partial, count, float(mean_rows) if mean_rows else 0.0), rest)
-    op = _B.REDUCE_MEAN if mean_rows else _B.REDUCE_SUM
-
-    def backward(g):
-        if mean_rows:
-            # g / R_global then broadcast: scale by the GLOBAL row count
-            scaled = be.binary_scalar(g._impl.storage, count, float(mean_rows), _B.DIV)
-            return [_out(be.reduce_axis_backward(_B.REDUCE_SUM, scaled, None, 1, rows_local, count), shape)]
-        return [_out(be.reduce_axis_backward(op, g._impl.storage, None, 1, rows_local, count), shape)]
-
-    _attach(out, [x], backward)
-    return out
+    _abi.call("vc_cuda_reduce_axis_partial", _B.REDUCE_SUM, _p(x), ctypes.c_size_t(1), ctypes.c_size_t(rows_local),
+              ctypes.c_size_t(count), ctypes.c_int64(0), 0, _p(partial), None, None)
+    return _combine_sums(comm, partial, count, float(mean_rows) if mean_rows else 0.0)
 
 
-def max_axis0(x: Tensor, comm: Communicator, shard: RowShard):
-    """Max over the sharded leading axis and its global argmax (int64 numpy
-    array), with the reference's scan semantics across shards (first maximal
-    row wins; a NaN only wins at global row 0). Not differentiable here."""
-    _require_cuda(x)
-    shape = x._impl.shape
-    rows_local, rest = shape[0], tuple(shape[1:])
-    count = int(np.prod(rest, dtype=np.int64))
+def sum_axis0_backward(g: CudaStorage, rows_local: int, count: int, mean_rows: int = 0) -> CudaStorage:
+    """dx [rows_local, count] of sum_axis0 for the upstream g [count]: g + 0
+    broadcast over this rank's rows (g / R_global + 0 for the mean, scaled by
+    the GLOBAL row count)."""
+    be = _be()
+    if mean_rows:
+        g = be.binary_scalar(g, count, float(mean_rows), _B.DIV)
+    return be.reduce_axis_backward(_B.REDUCE_SUM, g, None, 1, rows_local, count)
+
+
+def max_axis0(x: CudaStorage, rows_local: int, count: int, comm: Communicator, shard: RowShard):
+    """Max over the sharded leading axis of x [rows_local, count] and its
+    global argmax (int64), with the reference's scan semantics across
+    shards: the first maximal row wins (a lower rank wins ties) and a NaN
+    only wins at global row 0. Returns (values [count], indices [count])."""
     pv, pi = CudaStorage(count), CudaStorage(count, np.int64)
-    _abi.call("vc_cuda_reduce_axis_partial", _B.REDUCE_MAX, _p(x._impl.storage), ctypes.c_size_t(1),
-              ctypes.c_size_t(rows_local), ctypes.c_size_t(count), ctypes.c_int64(shard.start),
-              int(shard.rank > 0), None, _p(pv), _p(pi))
+    _abi.call("vc_cuda_reduce_axis_partial", _B.REDUCE_MAX, _p(x), ctypes.c_size_t(1), ctypes.c_size_t(rows_local),
+              ctypes.c_size_t(count), ctypes.c_int64(shard.start), int(shard.rank > 0), None, _p(pv), _p(pi))
     gv = comm.allgather(pv, count * 4, np.float32)
     gi = comm.allgather(pi, count * 8, np.int64)
     out, idx = CudaStorage(count), CudaStorage(count, np.int64)
     _abi.call("vc_cuda_combine_partials", _B.REDUCE_MAX, None, _p(gv), _p(gi), comm.world, ctypes.c_size_t(count),
               ctypes.c_float(0.0), 0, _p(out), _p(idx))
-    return _out(out, rest), _be().download(idx).reshape(rest)
+    return out, idx
 
 
-def sum_all(x: Tensor, comm: Communicator, mean_numel: int = 0) -> Tensor:
-    """Sum (or mean over `mean_numel` global elements) of every element of the
-    sharded tensor. Backward: the upstream broadcast over this rank's shard."""
-    _require_cuda(x)
-    be = _be()
-    n = x.numel
+def sum_all(x: CudaStorage, n_local: int, comm: Communicator, mean_numel: int = 0) -> CudaStorage:
+    """Sum (or the mean over `mean_numel` global elements) of every element
+    of the sharded tensor: one float, the same on every rank. The backward is
+    the upstream broadcast over this rank's shard (``broadcast_to``)."""
     partial = CudaStorage(1, np.float64)
-    _abi.call("vc_cuda_reduce_axis_partial", _B.REDUCE_SUM, _p(x._impl.storage), ctypes.c_size_t(1),
-              ctypes.c_size_t(n), ctypes.c_size_t(1), ctypes.c_int64(0), 0, _p(partial), None, None)
-    out = _out(_sum_over_shards(comm, partial, 1, float(mean_numel) if mean_numel else 0.0), ())
-    shape = x._impl.shape
-
-    def backward(g):
-        gs = g._impl.storage
-        if mean_numel:
-            gs = be.binary_scalar(gs, 1, float(mean_numel), _B.DIV)
-        return [_out(be.reduce_axis_backward(_B.REDUCE_SUM, gs, None, 1, n, 1), shape)]
-
-    _attach(out, [x], backward)
-    return out
+    _abi.call("vc_cuda_reduce_axis_partial", _B.REDUCE_SUM, _p(x), ctypes.c_size_t(1), ctypes.c_size_t(n_local),
+              ctypes.c_size_t(1), ctypes.c_int64(0), 0, _p(partial), None, None)
+    return _combine_sums(comm, partial, 1, float(mean_numel) if mean_numel else 0.0)
 
 
-def cross_entropy(logits: Tensor, targets, comm: Communicator, global_batch: int) -> Tensor:
+def cross_entropy(logits: CudaStorage, targets: CudaStorage, batch_local: int, classes: int,
+                  comm: Communicator, global_batch: int):
     """Mean softmax cross-entropy over a row-sharded batch: each rank's row
-    terms are summed on the device, the per-rank sums are combined in rank
-    order, and loss = -(sum) / global_batch. Backward is local (each row's
-    gradient needs only its own logits and the global batch size)."""
-    if logits.ndim != 2:
-        raise ValueError(f"cross_entropy expects [batch, classes] logits, got {logits.shape}")
-    _require_cuda(logits)
-    be = _be()
-    batch, classes = logits._impl.shape
-    tg = np.asarray(targets).astype(np.int64)
-    if tg.shape != (batch,):
-        raise ValueError(f"cross_entropy received {tg.size} targets for a batch of {batch}")
-    bad = (tg < 0) | (tg >= classes)
-    if bad.any():
-        raise IndexError(f"target class {int(tg[bad][0])} is out of range for {classes} classes")
-    dt = be.upload(tg)
-    _, m, s, part = be.cross_entropy(logits._impl.storage, dt, batch, classes, global_batch)
-    out = _out(_sum_over_shards(comm, part, 1, float(global_batch), negate=True), ())
-    x = logits.detach()
-
-    def backward(g):
-        return [_out(be.cross_entropy_backward(x._impl.storage, dt, m, s, g._impl.storage, batch, classes,
-                                               global_batch), (batch, classes))]
-
-    _attach(out, [logits], backward)
-    return out
+    terms are summed on the device, the per-rank sums combined in rank order,
+    loss = -(sum) / global_batch. Returns (loss, row_max, row_sum); the
+    backward is local: ``cross_entropy_backward`` with the same
+    global_batch."""
+    _, m, s, part = _be().cross_entropy(logits, targets, batch_local, classes, global_batch)
+    return _combine_sums(comm, part, 1, float(global_batch), negate=True), m, s
 
 
-__all__ = ["RowShard", "Communicator", "exchange_unique_id", "sum_axis0", "max_axis0", "sum_all", "cross_entropy"]
+def cross_entropy_backward(logits, targets, row_max, row_sum, upstream, batch_local, classes, global_batch):
+    return _be().cross_entropy_backward(logits, targets, row_max, row_sum, upstream, batch_local, classes,
+                                        global_batch)
+
+
+def binary_backward(op: int, a: CudaStorage, a_shape, b: CudaStorage, b_shape, g: CudaStorage, g_shape,
+                    comm: Communicator):
+    """Gradients of out = a (op) b when a and g are sharded along the leading
+    axis and b is replicated (broadcast along it, e.g. a bias, or config 5's
+    b [1,Q,1,L]): da is local; db sums over every rank's rows, so each rank
+    writes an unrounded double partial in the same fused pass and the
+    partials are combined in rank order. Returns (da, db), db identical on
+    every rank."""
+    da = CudaStorage(int(np.prod(a_shape, dtype=np.int64)))
+    nb = int(np.prod(b_shape, dtype=np.int64))
+    da_part, db_part = CudaStorage(da.size, np.float64), CudaStorage(nb, np.float64)
+    sa, ra = _abi.shape_arg(a_shape)
+    sb, rb = _abi.shape_arg(b_shape)
+    sg, rg = _abi.shape_arg(g_shape)
+    _abi.call("vc_cuda_binary_backward_partial", op, _p(a), sa, ra, _p(b), sb, rb, _p(g), sg, rg, _p(da_part),
+              _p(db_part))
+    # da has no cross-rank sum: round this rank's partial (one combine of one rank)
+    _abi.call("vc_cuda_combine_partials", _B.REDUCE_SUM, _p(da_part), None, None, 1, ctypes.c_size_t(da.size),
+              ctypes.c_float(0.0), 0, _p(da), None)
+    return da, _combine_sums(comm, db_part, nb)
+
+
+def bias_relu_sum(x: CudaStorage, b: CudaStorage, rows_local: int, cols: int, comm: Communicator) -> CudaStorage:
+    """relu(x + b).sum() of a row-sharded x [rows_local, cols] and a
+    replicated bias b [cols]: the fused forward's double partial per rank,
+    combined in rank order."""
+    part = CudaStorage(1, np.float64)
+    _abi.call("vc_cuda_bias_relu_sum", _p(x), _p(b), ctypes.c_size_t(rows_local), ctypes.c_size_t(cols), None,
+              _p(part))
+    return _combine_sums(comm, part, 1)
+
+
+def bias_relu_sum_backward(x, b, upstream, rows_local: int, cols: int, comm: Communicator):
+    """(dx, db) of the sharded relu(x + b).sum(): dx local (bit-exact with one
+    GPU), db from per-rank double partials combined in rank order."""
+    dx = CudaStorage(rows_local * cols)
+    part = CudaStorage(cols, np.float64)
+    _abi.call("vc_cuda_bias_relu_sum_backward", _p(x), _p(b), _p(upstream), ctypes.c_size_t(rows_local),
+              ctypes.c_size_t(cols), _p(dx), None, _p(part))
+    return dx, _combine_sums(comm, part, cols)
+
+
+__all__ = ["RowShard", "Communicator", "exchange_unique_id", "sum_axis0", "sum_axis0_backward", "max_axis0", "sum_all", "cross_entropy", "cross_entropy_backward", "binary_backward",
+           "bias_relu_sum", "bias_relu_sum_backward"]
