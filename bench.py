@@ -5,21 +5,33 @@
 
 Metric: effective HBM GB/s per op and elements/s. A step is
 one pass of the hot path over one batch of the workload; `value` = the sum of
-the ops' ALGORITHMIC bytes (count-once traffic, benchmark table) / device time
-of the step, from CUDA events on the library's stream, max over ranks.
+the ops' ALGORITHMIC bytes (count-once traffic, benchmark table) over all
+ranks / device time of the step, from CUDA events on the library's stream,
+max over ranks.
 
 Default workload (the one the driver runs): benchmark configuration 2 -- the
 same-shape elementwise sweep on a, b, g of [16384, 16384] float32 (2^28
 elements, 1.07 GB each, larger than the 126 MB L2, and L2 flushed before
 every timed op by a 256 MiB read): add, sub, mul, div, neg, exp, log, relu,
-sigmoid and a * 0.5, each
-forward and backward. Multi-GPU: weak scaling, each rank runs the sweep on its
-own [16384, 16384] shard of a leading-axis-sharded tensor (elementwise work
-needs no communication).
+sigmoid and a * 0.5, each forward and backward. Multi-GPU: strong scaling,
+as configuration 2 states -- ONE global [16384, 16384] tensor sharded along
+axis 0, rank r computing its 16384/N rows (elementwise work needs no
+communication). The global tensors are generated block-wise (1024-row blocks,
+each from its own seed) so every N sees the same data.
 
-The other workloads (configurations 1, 3, 4, 5) report the same metric per op
-for the reductions, the softmax family / cross-entropy and the strided
-broadcast. `--rows` shrinks the leading dimension (small profiling cases).
+The same line carries
+* `sharded_reduction`: configuration 3's axis-0 sum, max / argmax and full
+  sum over a row-sharded [8192, 32768] at N GPUs -- per-rank partials, the
+  CUDA device's NCCL all-gather, rank-order combine -- timed, split into the
+  local reduction and the collective + combine, and checked on every rank
+  against the 1-GPU result;
+* `per_config` (N = 1): per-op GB/s of configurations 1, 3, 4 and 5;
+* `e2e`: the sweep through the C ABI with host buffers (uploads and the
+  result's download inside the timed region);
+* `cpu_baseline`: the reference's own CPU path on a bounded sample.
+
+`--workload cfg1|cfg3|cfg4|cfg5` makes another configuration the headline;
+`--rows` shrinks the leading dimension (small profiling cases).
 
 Only bench.py's cpu_baseline leg and the --impl reference arm touch oracle/
 (the reference's own CPU path compiled from its sources, oracle/_ref).
@@ -118,8 +130,9 @@ class ClockSampler:
 # Workloads. Each op: (name, algorithmic bytes, callable returning the outputs).
 # --------------------------------------------------------------------------------------
 class Ctx:
-    def __init__(self, be, B, abi, rank, rows, torch):
+    def __init__(self, be, B, abi, rank, rows, torch, world=1):
         self.be, self.B, self.abi, self.rank, self.rows, self.torch = be, B, abi, rank, rows, torch
+        self.world = world
         self.launches = 0
 
     def L(self, x, k=1):
@@ -136,15 +149,45 @@ class Ctx:
         return s
 
 
+GEN_BLOCK = 1024  # rows per generator block of the global tensors
+
+
+def block_rows(seed, r0, r1, cols, draw, block=GEN_BLOCK):
+    """Rows [r0, r1) of a global float32 tensor whose 1024-row block k is
+    draw(default_rng([seed, k]), size): any rank can produce exactly its
+    shard, and every shard layout sees the same global tensor."""
+    out = np.empty((r1 - r0, cols), np.float32)
+    for k in range(r0 // block, (r1 + block - 1) // block if r1 > r0 else r0 // block):
+        lo, hi = k * block, (k + 1) * block
+        vals = draw(np.random.default_rng([seed, k]), (block, cols)).astype(np.float32)
+        a, b = max(lo, r0), min(hi, r1)
+        out[a - r0:b - r0] = vals[a - lo:b - lo]
+    return out
+
+
+def uniform_rows(seed, lo, hi, r0, r1, cols):
+    return block_rows(seed, r0, r1, cols, lambda g, size: g.uniform(lo, hi, size=size))
+
+
+def normal_rows(seed, std, r0, r1, cols):
+    return block_rows(seed, r0, r1, cols, lambda g, size: g.normal(0.0, std, size=size))
+
+
+CFG2_ROWS, CFG2_COLS = 16384, 16384
+
+
 def wl_cfg2(c: Ctx):
     be, B = c.be, c.B
-    rows = c.rows or 16384
-    cols = 16384
+    from vectorcore_b200.dist import RowShard
+
+    cols = CFG2_COLS
+    sh = RowShard(c.rows or CFG2_ROWS, c.world, c.rank)
+    rows = sh.count
     n = rows * cols
     shape = (rows, cols)
-    a_np = np.random.default_rng(2 + 100 * c.rank).uniform(0.1, 2.0, size=n).astype(np.float32)
-    b_np = np.random.default_rng(3 + 100 * c.rank).uniform(0.1, 2.0, size=n).astype(np.float32)
-    g_np = np.random.default_rng(9 + 100 * c.rank).uniform(-1.0, 1.0, size=n).astype(np.float32)
+    a_np = uniform_rows(2, 0.1, 2.0, sh.start, sh.stop, cols).reshape(-1)
+    b_np = uniform_rows(3, 0.1, 2.0, sh.start, sh.stop, cols).reshape(-1)
+    g_np = uniform_rows(9, -1.0, 1.0, sh.start, sh.stop, cols).reshape(-1)
     a, b, g = be.upload(a_np), be.upload(b_np), be.upload(g_np)
     s_neg = be.binary_scalar(a, n, 1.0, B.SUB)  # a - 1: signed inputs for neg / relu / sigmoid
     saved = {}
@@ -178,12 +221,13 @@ def wl_cfg2(c: Ctx):
     ]
     host = {"a": a_np, "b": b_np, "g": g_np}
     dev = {"a": a, "b": b, "g": g}
-    desc = (f"cfg2: same-shape elementwise sweep, a,b,g [{rows},{cols}] f32 per GPU, "
-            "add/sub/mul/div/neg/exp/log/relu/sigmoid/a*0.5 fwd+bwd")
+    desc = (f"cfg2: same-shape elementwise sweep, a,b,g [{sh.rows},{cols}] f32 sharded along axis 0 "
+            f"({rows} rows per GPU), add/sub/mul/div/neg/exp/log/relu/sigmoid/a*0.5 fwd+bwd")
     # first op that reads each uploaded input (g only from the backward ops on)
     first_use = {"a": 0, "b": 0, "g": [name for name, _, _ in ops].index("sub.bwd")}
-    return {"ops": ops, "elements": n, "desc": desc, "host": host, "dev": dev, "e2e_result": "last",
-            "first_use": first_use, "metric": "effective HBM GB/s (config 2 elementwise sweep, fwd+bwd)"}
+    return {"ops": ops, "elements": n, "elements_global": sh.rows * cols, "desc": desc, "host": host, "dev": dev,
+            "e2e_result": "last", "first_use": first_use,
+            "metric": "effective HBM GB/s (config 2 elementwise sweep, fwd+bwd)"}
 
 
 def wl_cfg1(c: Ctx):
@@ -336,6 +380,56 @@ WORKLOADS = {"cfg1": wl_cfg1, "cfg2": wl_cfg2, "cfg3": wl_cfg3, "cfg4": wl_cfg4,
 # --------------------------------------------------------------------------------------
 # Our arm
 # --------------------------------------------------------------------------------------
+class Timer:
+    """Per-op CUDA events on the library's stream, with an L2 flush (a read of
+    256 MiB) before every timed op unless the workload is L2-resident by
+    design (configuration 1)."""
+
+    def __init__(self, torch, vstream, flush_l2=True):
+        self.torch, self.vstream = torch, vstream
+        self.flush_buf = torch.ones(64 << 20, dtype=torch.float32, device="cuda") if flush_l2 else None
+        self.flush_out = torch.empty((), dtype=torch.float32, device="cuda")
+
+    def flush(self):
+        if self.flush_buf is not None:
+            with self.torch.cuda.stream(self.vstream):
+                self.torch.sum(self.flush_buf, dim=0, out=self.flush_out)
+
+    def run(self, ops, steps, warmup, barrier):
+        """Per-op device milliseconds summed over `steps` timed steps."""
+        torch = self.torch
+        for _ in range(warmup):
+            for _, _, fn in ops:
+                fn()
+        barrier()
+        ev = [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in ops]
+        per_op_ms = [0.0] * len(ops)
+        for _ in range(steps):
+            # keep the GPU busy while the host queues the step, so the first
+            # op's events do not include host launch latency
+            with torch.cuda.stream(self.vstream):
+                torch.cuda._sleep(400_000)
+            for i, (_, _, fn) in enumerate(ops):
+                self.flush()
+                ev[i][0].record(self.vstream)
+                fn()
+                ev[i][1].record(self.vstream)
+            torch.cuda.synchronize()
+            for i in range(len(ops)):
+                per_op_ms[i] += ev[i][0].elapsed_time(ev[i][1])
+        barrier()
+        return per_op_ms
+
+
+def release(be, torch):
+    """Hand cached device memory back between workloads."""
+    be.synchronize()
+    from vectorcore_b200 import _abi
+
+    _abi.call("vc_cuda_pool_trim")
+    torch.cuda.empty_cache()
+
+
 def run_ours(args):
     import torch
 
@@ -351,73 +445,36 @@ def run_ours(args):
 
         import torch.distributed as dist
 
-        # The sweep has no data-path collective (each rank owns a row shard);
-        # the process group only carries the barrier and the max-over-ranks of
-        # the timings, on the host after a CUDA synchronise, so gloo suffices
-        # (and keeps NCCL's banner off stdout).
+        # The sweep has no data-path collective (each rank owns a row shard).
+        # The host group carries the barrier, the max-over-ranks of the
+        # timings and the NCCL unique id of the CUDA device's communicator
+        # (the sharded reductions' all-gather runs over NCCL, not this group).
         torch.cuda.set_device(local)
         dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
     _abi.check(_abi.lib.vc_cuda_init(local))
     torch.cuda.set_device(local)
     be = B.CudaBackend.instance()
     vstream = torch.cuda.ExternalStream(_abi.lib.vc_cuda_stream())
-    ctx = Ctx(be, B, _abi, rank, args.rows, torch)
+    ctx = Ctx(be, B, _abi, rank, args.rows, torch, world)
     wl = WORKLOADS[args.workload](ctx)
     torch.cuda.empty_cache()  # inputs generated with torch now live in the library's pool
     ops = wl["ops"]
     n = wl["elements"]
-
-    # L2 flush before every timed op (not for configuration 1, whose working
-    # set stays in L2 by design): a read of a 256 MiB buffer leaves the 126 MB
-    # L2 holding clean lines of that buffer, so no op reads the tail of an
-    # input the previous op left in L2, and the previous op's dirty output
-    # lines are written back before the next op's start event.
-    flush_buf = None
-    if args.workload != "cfg1":
-        flush_buf = torch.ones(64 << 20, dtype=torch.float32, device="cuda")
-        flush_out = torch.empty((), dtype=torch.float32, device="cuda")
-
-    def flush():
-        with torch.cuda.stream(vstream):
-            torch.sum(flush_buf, dim=0, out=flush_out)
-
-    def step(events=None):
-        outs = []
-        if events is not None:
-            # Keep the GPU busy for ~200 us while the host queues the step,
-            # so the first op's events do not include host launch latency.
-            with torch.cuda.stream(vstream):
-                torch.cuda._sleep(400_000)
-        for i, (_, _, fn) in enumerate(ops):
-            if events is not None:
-                if flush_buf is not None:
-                    flush()
-                events[i][0].record(vstream)
-            outs.append(fn())
-            if events is not None:
-                events[i][1].record(vstream)
-        return outs
 
     def barrier():
         if dist is not None:
             dist.barrier()
         torch.cuda.synchronize()
 
-    for _ in range(args.warmup):
-        step()
-    barrier()
+    timer = Timer(torch, vstream, flush_l2=args.workload != "cfg1")
+    # warm-up, then the timed steps (launches counted in the timed steps only)
+    timer.run(ops, 0, args.warmup, barrier)
     ctx.launches = 0
-    ev = [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in ops]
-    per_op_ms = [0.0] * len(ops)
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         barrier()
         start.record(vstream)
-        for _ in range(args.steps):
-            step(ev)
-            torch.cuda.synchronize()
-            for i in range(len(ops)):
-                per_op_ms[i] += ev[i][0].elapsed_time(ev[i][1])
+        per_op_ms = timer.run(ops, args.steps, 0, barrier)
         stop.record(vstream)
         barrier()
     total_ms = start.elapsed_time(stop)
@@ -427,8 +484,10 @@ def run_ours(args):
     if dist is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     step_ms = float(t.item())
-    bytes_per_step = sum(nb for _, nb, _ in ops)
-    value = world * bytes_per_step / (step_ms * 1e-3) / 1e9
+    bytes_per_step = sum(nb for _, nb, _ in ops)  # this rank's
+    n_global = wl.get("elements_global", world * n)
+    bytes_global = bytes_per_step * n_global / n
+    value = bytes_global / (step_ms * 1e-3) / 1e9
     per_op = {name: {"ms": round(per_op_ms[i] / args.steps, 4),
                      "gbs": round(nb / (per_op_ms[i] / args.steps * 1e-3) / 1e9, 1)}
               for i, (name, nb, _) in enumerate(ops)}
@@ -450,8 +509,23 @@ def run_ours(args):
     if not args.no_e2e and "host" in wl:
         # a second device set of the same inputs for the double-buffered loop
         wl2 = WORKLOADS[args.workload](ctx)
-        e2e = measure_e2e(args, [wl, wl2], barrier, dist, torch, bytes_per_step, world, n)
+        e2e = measure_e2e(args, [wl, wl2], barrier, dist, torch, bytes_global, world, n)
         del wl2
+    desc, metric, nops = wl["desc"], wl["metric"], len(ops)
+    del wl, ops
+    release(be, torch)
+
+    sharded = None
+    if not args.no_sharded:
+        sharded = sharded_reduction(args, ctx, timer, barrier, dist, world, rank)
+        release(be, torch)
+
+    per_config = None
+    if world == 1 and not args.no_per_config and args.workload == "cfg2" and not args.rows:
+        per_config = {}
+        for name in ("cfg1", "cfg3", "cfg4", "cfg5"):
+            per_config[name] = measure_config(name, ctx, torch, vstream, args, barrier)
+            release(be, torch)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "cfg2":
@@ -463,7 +537,7 @@ def run_ours(args):
     if rank != 0:
         return
     line = {
-        "metric": wl["metric"],
+        "metric": metric,
         "value": round(value, 1),
         "unit": "GB/s",
         "n_gpus": world,
@@ -471,16 +545,18 @@ def run_ours(args):
         "warmup": args.warmup,
         "ms_per_step": round(step_ms, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if args.workload == "cfg2" else "weak",
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic (seeded generators with the benchmark table's shapes and distributions)",
-        "config": {"workload": wl["desc"], "elements_per_gpu": n,
+        "config": {"workload": desc, "elements_global": n_global,
+                   "elements_per_gpu": n,
                    "l2": "inputs larger than the 126 MB L2, and L2 flushed before every timed op (a 256 MiB read)"
                    if args.workload != "cfg1"
                    else "16.8 MB working set stays in L2 by design (launch-bound configuration)",
-                   "parallelism": f"leading-axis shards x{world}, no communication"},
-        "elements_per_s": round(world * len(ops) * n / (step_ms * 1e-3), 1),
+                   "parallelism": f"axis-0 shards of the global tensor over {world} GPU(s), no data-path "
+                                  "communication" if args.workload == "cfg2" else f"replicas x{world}"},
+        "elements_per_s": round(nops * n_global / (step_ms * 1e-3), 1),
         "pct_of_peak": round(100 * value / world / peak, 1),
         "per_op": per_op,
         "roofline": {"bound": "hbm", "kernel": dom_name, "achieved": round(achieved, 1), "peak": peak,
@@ -491,12 +567,132 @@ def run_ours(args):
         "gpu_launches": gpu_launches,
         "e2e": e2e,
         "cpu_baseline": cpu,
+        "sharded_reduction": sharded,
+        "per_config": per_config,
         "wall_ms_timed_region": round(total_ms, 2),
     }
     print(json.dumps(line), flush=True)
 
 
-def measure_e2e(args, sets, barrier, dist, torch, bytes_per_step, world, n):
+def wl_metric(name):
+    return {"cfg1": "effective GB/s (config 1 bias+relu+sum, fwd+bwd)",
+            "cfg2": "effective HBM GB/s (config 2 elementwise sweep, fwd+bwd)",
+            "cfg3": "effective HBM GB/s (config 3 reductions, fwd+bwd)",
+            "cfg4": "effective HBM GB/s (config 4 softmax / cross-entropy, fwd+bwd)",
+            "cfg5": "effective HBM GB/s (config 5 strided broadcast multiply, fwd+bwd)"}[name]
+
+
+def measure_config(name, ctx, torch, vstream, args, barrier):
+    """Per-op GB/s of another configuration at its full shape on this GPU
+    (same timing rules as the headline: warm-up, CUDA events, L2 flush)."""
+    wl = WORKLOADS[name](ctx)
+    torch.cuda.empty_cache()
+    ops = wl["ops"]
+    steps = max(1, min(args.steps, 5))
+    per_op_ms = Timer(torch, vstream, flush_l2=name != "cfg1").run(ops, steps, 3, barrier)
+    step_ms = sum(per_op_ms) / steps
+    nbytes = sum(nb for _, nb, _ in ops)
+    peak, _ = hbm_peak()
+    res = {"metric": wl_metric(name), "workload": wl["desc"], "steps": steps, "warmup": 3,
+           "ms_per_step": round(step_ms, 4), "value": round(nbytes / (step_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+           "per_op": {op: {"ms": round(per_op_ms[i] / steps, 4),
+                           "gbs": round(nb / (per_op_ms[i] / steps * 1e-3) / 1e9, 1),
+                           "frac": round(nb / (per_op_ms[i] / steps * 1e-3) / 1e9 / peak, 3)}
+                      for i, (op, nb, _) in enumerate(ops)}}
+    if name == "cfg1":
+        res["us_per_step"] = round(step_ms * 1e3, 2)
+    return res
+
+
+def sharded_reduction(args, ctx, timer, barrier, dist, world, rank):
+    """Configuration 3's reductions over the sharded axis at `world` GPUs:
+    x [8192, 32768] ~ N(0,1) row-sharded; per step the axis-0 sum, the
+    axis-0 max with its argmax and the full sum, each as a per-rank partial
+    (vc_cuda_reduce_axis_partial), the CUDA device's NCCL all-gather and the
+    rank-order combine (vc_cuda_combine_partials). Timed with CUDA events
+    (max over ranks); a second loop times the local partials alone, so the
+    difference is the collective + combine. Every rank checks its results
+    against the 1-GPU reduction of the whole tensor (computed on rank 0):
+    bit for bit for max / argmax, within 1e-5 for the sums."""
+    import torch
+
+    from vectorcore_b200 import dist as vdist
+
+    be, B, abi = ctx.be, ctx.B, ctx.abi
+    rows, cols = 8192, 32768
+    sh = vdist.RowShard(rows, world, rank)
+    xl = be.upload(normal_rows(4, 1.0, sh.start, sh.stop, cols))
+    if world > 1:
+        comm = vdist.Communicator.from_torch(timeout_ms=120_000)
+    else:
+        comm = vdist.Communicator(1, 0, vdist.Communicator.unique_id(), timeout_ms=120_000)
+    res = {}
+
+    def full_op():
+        res["sum0"] = vdist.sum_axis0(xl, sh.count, cols, comm)
+        res["max0"] = vdist.max_axis0(xl, sh.count, cols, comm, sh)
+        res["sum"] = vdist.sum_all(xl, sh.count * cols, comm)
+
+    def p(st):
+        return None if st is None else ctypes.c_void_p(st.ptr)
+
+    ps, pv, pi, pt = (be.allocate(cols, np.float64), be.allocate(cols), be.allocate(cols, np.int64),
+                      be.allocate(1, np.float64))
+
+    def local_op():
+        abi.call("vc_cuda_reduce_axis_partial", B.REDUCE_SUM, p(xl), ctypes.c_size_t(1), ctypes.c_size_t(sh.count),
+                 ctypes.c_size_t(cols), ctypes.c_int64(0), 0, p(ps), None, None)
+        abi.call("vc_cuda_reduce_axis_partial", B.REDUCE_MAX, p(xl), ctypes.c_size_t(1), ctypes.c_size_t(sh.count),
+                 ctypes.c_size_t(cols), ctypes.c_int64(sh.start), int(sh.rank > 0), None, p(pv), p(pi))
+        abi.call("vc_cuda_reduce_axis_partial", B.REDUCE_SUM, p(xl), ctypes.c_size_t(1),
+                 ctypes.c_size_t(sh.count * cols), ctypes.c_size_t(1), ctypes.c_int64(0), 0, p(pt), None, None)
+
+    steps = max(1, args.steps)
+    ms_full = timer.run([("sharded", 0, full_op)], steps, max(3, args.warmup), barrier)[0] / steps
+    ms_local = timer.run([("local", 0, local_op)], steps, 3, barrier)[0] / steps
+    comm.synchronize()
+    t = torch.tensor([ms_full, ms_local], dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_full, ms_local = float(t[0]), float(t[1])
+    got = {"sum0": be.download(res["sum0"]), "max0": be.download(res["max0"][0]),
+           "arg0": be.download(res["max0"][1]), "sum": be.download(res["sum"])}
+    # the 1-GPU results of the whole tensor, on rank 0
+    expect = [None]
+    if rank == 0:
+        xf = be.upload(normal_rows(4, 1.0, 0, rows, cols))
+        v, i = be.reduce_axis(xf, 1, rows, cols, B.REDUCE_MAX, want_index=True)
+        expect[0] = {"sum0": be.download(be.reduce_axis(xf, 1, rows, cols, B.REDUCE_SUM)), "max0": be.download(v),
+                     "arg0": be.download(i), "sum": be.download(be.reduce_sum(xf, rows * cols))}
+        del xf
+    if dist is not None:
+        dist.broadcast_object_list(expect, src=0)
+    e = expect[0]
+    ok = {"sum_axis0": bool(np.allclose(got["sum0"], e["sum0"], rtol=1e-5, atol=1e-5 * np.sqrt(rows))),
+          "max_axis0_bitexact": bool(np.array_equal(got["max0"].view(np.uint32), e["max0"].view(np.uint32))),
+          "argmax_axis0": bool(np.array_equal(got["arg0"], e["arg0"])),
+          "sum_all": bool(abs(float(got["sum"][0]) - float(e["sum"][0])) <= 1e-5 * np.sqrt(rows * cols))}
+    oks = [ok]
+    if dist is not None:
+        oks = [None] * world
+        dist.all_gather_object(oks, ok)
+    comm.close()
+    n_global = rows * cols
+    nbytes = 3 * 4 * n_global  # each of the three reductions reads the global tensor once
+    return {"workload": f"cfg3: x [{rows},{cols}] f32 sharded along axis 0 over {world} GPU(s) ({sh.count} rows "
+                        "on rank 0): axis-0 sum, axis-0 max+argmax, full sum -- per-rank partials, NCCL "
+                        "all-gather, rank-order combine",
+            "n_gpus": world, "steps": steps, "ms_per_step": round(ms_full, 4),
+            "value": round(nbytes / (ms_full * 1e-3) / 1e9, 1), "unit": "GB/s",
+            "elements_per_s": round(3 * n_global / (ms_full * 1e-3), 1),
+            "local_reduce_ms": round(ms_local, 4),
+            "collective_and_combine_ms": round(max(0.0, ms_full - ms_local), 4),
+            "limiter": ("collective + combine" if ms_full - ms_local > ms_local else "local reduction"),
+            "collective": f"NCCL all-gather over {world} rank(s) (vc_cuda_comm_allgather)",
+            "matches_1gpu": {f"rank{r}": o for r, o in enumerate(oks)}}
+
+
+def measure_e2e(args, sets, barrier, dist, torch, bytes_global, world, n):
     """The same step through the public API with host buffers: every step
     uploads its inputs from page-locked host memory and reads its final
     result back. The copies are asynchronous (vc_cuda_upload_async /
@@ -556,8 +752,9 @@ def measure_e2e(args, sets, barrier, dist, torch, bytes_per_step, world, n):
     for p in pins.values():
         p.close()
     out_pin.close()
-    return {"value": round(world * bytes_per_step / secs / 1e9, 2), "unit": "GB/s",
-            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": n * 4, "steps": steps,
+    return {"value": round(bytes_global / secs / 1e9, 2), "unit": "GB/s",
+            "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": n * 4 * world,
+            "h2d_bytes_per_step_per_gpu": h2d, "d2h_bytes_per_step_per_gpu": n * 4, "steps": steps,
             "note": "page-locked host inputs uploaded and the step's last gradient read back every step through "
                     "the C ABI: asynchronous copies, inputs double-buffered (the next step's upload overlaps this "
                     "step's compute), each op waits only for the inputs it reads"}
@@ -599,13 +796,16 @@ def reference_sweep_once(vc, a, b, g, a1):
             t.zero_grad()
 
 
-def _ref_inputs(vc):
-    r, c = REF_SAMPLE
-    a = vc.Tensor(np.random.default_rng(2).uniform(0.1, 2.0, (r, c)).astype(np.float32), requires_grad=True)
-    b = vc.Tensor(np.random.default_rng(3).uniform(0.1, 2.0, (r, c)).astype(np.float32), requires_grad=True)
-    g = vc.Tensor(np.random.default_rng(9).uniform(-1.0, 1.0, (r, c)).astype(np.float32))
-    a1 = vc.Tensor((np.random.default_rng(2).uniform(0.1, 2.0, (r, c)) - 1.0).astype(np.float32),
-                   requires_grad=True)
+def _ref_inputs(vc, rows):
+    """The first `rows` rows of the benchmark's global a, b, g (the same
+    block-wise generators as our arm) as the reference's own tensors; a1 =
+    a - 1 is the signed input of neg / relu / sigmoid."""
+    c = CFG2_COLS
+    a_np = uniform_rows(2, 0.1, 2.0, 0, rows, c)
+    a = vc.Tensor(a_np, requires_grad=True)
+    b = vc.Tensor(uniform_rows(3, 0.1, 2.0, 0, rows, c), requires_grad=True)
+    g = vc.Tensor(uniform_rows(9, -1.0, 1.0, 0, rows, c))
+    a1 = vc.Tensor(a_np - np.float32(1.0), requires_grad=True)
     return a, b, g, a1
 
 
@@ -622,7 +822,7 @@ def reference_cpu_sample(repeats=2):
     vc, why = _ref_module()
     if vc is None:
         return {"value": None, "unit": "GB/s", "cores": os.cpu_count(), "kind": "reference", "sample": why}
-    a, b, g, a1 = _ref_inputs(vc)
+    a, b, g, a1 = _ref_inputs(vc, REF_SAMPLE[0])
     reference_sweep_once(vc, a, b, g, a1)  # warm-up (page faults, pool threads)
     times = []
     for _ in range(repeats):
@@ -638,6 +838,10 @@ def reference_cpu_sample(repeats=2):
 
 
 def run_reference(args):
+    """The reference's own CPU path (its pybind11 module over its thread
+    pool, compiled from its sources into oracle/_ref) on the full
+    configuration-2 workload: the [16384, 16384] sweep, forward and backward
+    through its public Python API. Rank 0 alone runs it."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -646,27 +850,29 @@ def run_reference(args):
     if vc is None:
         print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
         return
-    a, b, g, a1 = _ref_inputs(vc)
+    rows = args.rows or CFG2_ROWS
+    a, b, g, a1 = _ref_inputs(vc, rows)
     for _ in range(args.warmup):
         reference_sweep_once(vc, a, b, g, a1)
     t0 = time.perf_counter()
     for _ in range(args.steps):
         reference_sweep_once(vc, a, b, g, a1)
     secs = (time.perf_counter() - t0) / args.steps
-    n = REF_SAMPLE[0] * REF_SAMPLE[1]
+    n = rows * CFG2_COLS
     value = SWEEP_BYTES_PER_ELEMENT * n / secs / 1e9
     threads = _ref_threads()
     line = {
         "impl": "reference",
         "metric": "effective HBM GB/s (config 2 elementwise sweep, fwd+bwd)",
         "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(secs * 1e3, 2), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32", "data": "synthetic (numpy default_rng seeds 2/3/9)",
-        "config": {"workload": "cfg2: same-shape elementwise sweep fwd+bwd on the reference's CPU path, a "
-                               f"[{REF_SAMPLE[0]},{REF_SAMPLE[1]}] sample of each [16384,16384] tensor",
-                   "elements": n},
+        "ms_per_step": round(secs * 1e3, 2), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (the same block-wise seeded generators as our arm)",
+        "config": {"workload": f"cfg2: same-shape elementwise sweep, a,b,g [{rows},{CFG2_COLS}] f32, "
+                               "add/sub/mul/div/neg/exp/log/relu/sigmoid/a*0.5 fwd+bwd, on the reference's CPU "
+                               "path (its thread pool on the host's cores)",
+                   "elements_global": n},
         "cpu_baseline": {"value": round(value, 2), "unit": "GB/s", "cores": threads, "kind": "reference",
-                         "sample": f"[{REF_SAMPLE[0]},{REF_SAMPLE[1]}] (2^26 elements) per step"},
+                         "sample": f"the full [{rows},{CFG2_COLS}] sweep per step"},
         "e2e": {"value": round(value, 2), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -682,6 +888,8 @@ def main():
     ap.add_argument("--rows", type=int, default=0, help="shrink the leading dimension (profiling cases)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sharded", action="store_true", help="skip the sharded-reduction block")
+    ap.add_argument("--no-per-config", action="store_true", help="skip the other configurations (N = 1)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
