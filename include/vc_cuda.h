@@ -30,8 +30,9 @@
  *    returns; callers never see it.
  *  - Results match the reference's CPU path: bit-exact for add, sub, mul,
  *    div, neg, relu, max and argmax (first index wins ties); within 2 ulp of
- *    glibc for exp, log and sigmoid (CUDA expf/logf); sums accumulate in
- *    double and round once, like cpu::sum / cpu::reduce_axis.
+ *    glibc for exp, log and sigmoid (a table-driven float exponential of this
+ *    library, CUDA's logf); sums accumulate in double and round once, like
+ *    cpu::sum / cpu::reduce_axis.
  *
  * Status codes map onto the reference's exception types
  * (src/ops.cpp, src/shape.cpp): invalid_argument -> VC_ERR_INVALID,
@@ -315,7 +316,10 @@ vc_status vc_cuda_graph_destroy(void* graph);
 
 /* loss[0] = float(sum of relu(x + b)); loss_partial[0] (optional) = the
  * unrounded double sum (a shard's partial). Either output may be null, not
- * both. */
+ * both. The forward's last-CTA ticket is a counter owned by the stream the
+ * call is enqueued on, so calls in flight on different streams do not share
+ * it; a CUDA graph keeps the counter of the stream it was captured on, so
+ * replay one graph on one stream at a time. */
 vc_status vc_cuda_bias_relu_sum(const float* x, const float* b, size_t rows, size_t cols, float* loss,
                                 double* loss_partial);
 /* Given the upstream gradient u (device scalar) of the sum:
@@ -368,11 +372,28 @@ vc_status vc_cuda_comm_unique_id(void* id, size_t bytes);
 vc_status vc_cuda_comm_init(int nranks, int rank, const void* id, size_t bytes, int timeout_ms);
 /* recv [nranks * bytes_per_rank] = every rank's send, in rank order; enqueued. */
 vc_status vc_cuda_comm_allgather(const void* send, void* recv, size_t bytes_per_rank);
+/* `count` all-gathers (recvs[i] [nranks * bytes_per_rank[i]] = every rank's
+ * sends[i]) issued as ONE NCCL group: one launch and one enqueue wait for the
+ * partials of several reductions. Enqueued. */
+vc_status vc_cuda_comm_allgather_group(const void* const* sends, void* const* recvs, const size_t* bytes_per_rank,
+                                       int count);
 /* Wait for the stream with a deadline, watching the communicator for errors. */
 vc_status vc_cuda_comm_synchronize(int timeout_ms);
 vc_status vc_cuda_comm_destroy(void);
 int vc_cuda_comm_size(void);
 int vc_cuda_comm_rank(void);
+
+/* ---- failure detection -------------------------------------------------------
+ * No counterpart in the reference (its Metal errors arrive through command
+ * buffer completion handlers, src/metal/metal_backend.mm:545-549). */
+
+/* Enqueue a one-thread kernel that waits on an mbarrier nothing completes,
+ * using the bounded wait of the pipelined kernels limited to `polls` polls
+ * (each at most ~2 us): the wait gives up, records the timeout in the device
+ * error word and the kernel exits. The next blocking call (vc_cuda_download,
+ * vc_cuda_synchronize) then fails with VC_ERR_TIMEOUT and clears the error;
+ * the device stays usable. For tests of the failure path. 1 <= polls <= 2^21. */
+vc_status vc_cuda_selftest_wait_timeout(long long polls);
 
 /* ---- existing ops (correct, not tuned: off the bandwidth-bound path) ---- */
 

@@ -113,6 +113,7 @@ _SIGS = {
     "vc_cuda_matmul": (c_int, [_f, _f, _f, c_size_t, c_size_t, c_size_t, _szp, _szp, c_size_t, c_int, c_int]),
     "vc_cuda_transpose_last2": (c_int, [_f, _f, c_size_t, c_size_t, c_size_t]),
     "vc_cuda_reduce_sum_noalloc": (c_int, [_f, c_size_t, _f]),
+    "vc_cuda_selftest_wait_timeout": (c_int, [c_int64]),
     "vc_cuda_reduce_axis_partial": (c_int, [c_int, _f, c_size_t, c_size_t, c_size_t, c_int64, c_int, c_void_p,
                                             _f, c_void_p]),
     "vc_cuda_binary_backward_partial": (c_int, [c_int, _f, _szp, c_int, _f, _szp, c_int, _f, _szp, c_int, c_void_p,
@@ -122,6 +123,7 @@ _SIGS = {
     "vc_cuda_comm_unique_id": (c_int, [c_void_p, c_size_t]),
     "vc_cuda_comm_init": (c_int, [c_int, c_int, c_void_p, c_size_t, c_int]),
     "vc_cuda_comm_allgather": (c_int, [c_void_p, c_void_p, c_size_t]),
+    "vc_cuda_comm_allgather_group": (c_int, [POINTER(c_void_p), POINTER(c_void_p), _szp, c_int]),
     "vc_cuda_comm_synchronize": (c_int, [c_int]),
     "vc_cuda_comm_destroy": (c_int, []),
     "vc_cuda_comm_size": (c_int, []),

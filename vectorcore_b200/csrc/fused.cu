@@ -25,7 +25,7 @@ namespace vc {
 namespace {
 
 constexpr unsigned kThreads = 256;
-constexpr unsigned kTicketForward = 0;        // ticket counter slots
+constexpr unsigned kTicketForward = 0;        // slots among the stream's ticket counters
 constexpr unsigned kTicketBackward = 1;
 constexpr unsigned kFwdPerThread = 4;         // forward: float4 groups per thread (in flight together)
 // backward CTA: 64 float4 columns (256 floats) x 4 row groups x 4 rows
@@ -363,7 +363,7 @@ vc_status vc_cuda_bias_relu_sum(const float* x, const float* b, size_t rows, siz
     if (ctas > 0x7fffffffull) fail(VC_ERR_OVERFLOW, "bias_relu_sum: tensor too large");
     const bool cols_small = units < (1ull << 32) && cols_units < (1ull << 32);
     const FastDiv cols_fd(cols_small ? static_cast<unsigned>(cols_units) : 1u);
-    unsigned* ticket = counters() + kTicketForward;
+    unsigned* ticket = stream_tickets() + kTicketForward;
     if (vec && cols_small) {
         const unsigned long long wide = (units + kFwdPerCta - 1) / kFwdPerCta;
         Scratch partial(wide * sizeof(double));
@@ -409,7 +409,7 @@ vc_status vc_cuda_bias_relu_sum_backward(const float* x, const float* b, const f
     Scratch counts(cols * sizeof(unsigned));
     VC_CUDA(cudaMemsetAsync(counts.as<unsigned>(), 0, cols * sizeof(unsigned), stream()));
     const dim3 grid(static_cast<unsigned>(col_blocks), static_cast<unsigned>(segs));
-    unsigned* ticket = counters() + kTicketBackward;
+    unsigned* ticket = stream_tickets() + kTicketBackward;
     if (vec) bias_relu_sum_bwd<true><<<grid, kThreads, 0, stream()>>>(x, b, upstream, rows, cols, dx, db, db_partial, counts.as<unsigned>(), ticket);
     else bias_relu_sum_bwd<false><<<grid, kThreads, 0, stream()>>>(x, b, upstream, rows, cols, dx, db, db_partial, counts.as<unsigned>(), ticket);
     check_launch("bias_relu_sum_backward");

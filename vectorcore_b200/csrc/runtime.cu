@@ -273,6 +273,21 @@ thread_local std::vector<void*>* t_deferred_frees = nullptr;
 cudaStream_t stream() { return t_stream_override ? t_stream_override : state().stream; }
 int sm_count() { return state().sms; }
 unsigned* counters() { return state().counters; }
+
+unsigned* stream_tickets() {
+    static std::mutex m;
+    static std::unordered_map<cudaStream_t, unsigned> slots;
+    const cudaStream_t st = stream();
+    std::lock_guard<std::mutex> lock(m);
+    auto it = slots.find(st);
+    if (it == slots.end()) {
+        const std::size_t next = slots.size();
+        if ((next + 1) * kPerStreamTickets > kCounterSlots)
+            fail(VC_ERR_RUNTIME, "too many distinct streams for the per-stream ticket counters");
+        it = slots.emplace(st, static_cast<unsigned>(next)).first;
+    }
+    return state().counters + static_cast<std::size_t>(it->second) * kPerStreamTickets;
+}
 unsigned* device_error_word() { return state().error_word; }
 
 static void* pool_alloc(std::size_t bytes) {
@@ -444,6 +459,17 @@ void validate_rank(int rank, const char* what) {
                                  std::to_string(kMaxRank));
 }
 
+// One thread waits on an mbarrier whose phase nothing completes, with the
+// bounded wait of the pipelined kernels limited to `polls` polls: it gives
+// up, sets kErrWaitTimeout and returns (the failure path, without a fault).
+__global__ void selftest_wait_timeout_kernel(long long polls, unsigned* err) {
+    __shared__ unsigned long long bar;
+    if (threadIdx.x != 0) return;
+    mbar_init(&bar, 1);
+    mbar_fence_init();
+    mbar_wait_bounded(&bar, 0, err, polls);
+}
+
 static void surface_device_errors() {
     State& s = state();
     unsigned word = 0;
@@ -551,6 +577,15 @@ vc_status vc_cuda_free(void* pointer) {
     VC_API_BEGIN
     if (!state().ready) return VC_OK;
     pool_free(pointer);
+    VC_API_END
+}
+
+vc_status vc_cuda_selftest_wait_timeout(long long polls) {
+    VC_API_BEGIN
+    ensure_init();
+    if (polls < 1 || polls > kWaitPolls) fail(VC_ERR_OUT_OF_RANGE, "selftest_wait_timeout: polls must be in [1, 2^21]");
+    selftest_wait_timeout_kernel<<<1, 32, 0, stream()>>>(polls, device_error_word());
+    check_launch("selftest_wait_timeout_kernel");
     VC_API_END
 }
 

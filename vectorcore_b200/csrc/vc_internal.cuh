@@ -56,6 +56,11 @@ int bound_device();              // that GPU's index (-1 before initialisation)
 cudaStream_t stream();           // the enqueue stream
 int sm_count();
 unsigned* counters();            // zeroed ticket counters (kCounterSlots)
+// kPerStreamTickets zeroed counters owned by the current enqueue stream:
+// kernels that reset their ticket in-kernel use these, so calls in flight on
+// different streams never share a counter (calls on one stream are ordered).
+unsigned* stream_tickets();
+constexpr unsigned kPerStreamTickets = 4;
 unsigned* device_error_word();   // sticky device error bits
 void check_launch(const char* what);
 
@@ -231,12 +236,13 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned 
         : "memory");
     return ok != 0;
 }
-// Wait for phase `parity` with an iteration limit (at most kWaitPolls polls
-// of up to kWaitHintNs each, a few seconds); false (and the device error bit)
-// when it gave up.
+// Wait for phase `parity` with an iteration limit (at most `polls` polls of
+// up to kWaitHintNs each; the kernels use kWaitPolls, a few seconds); false
+// (and the device error bit) when it gave up.
 constexpr long long kWaitPolls = 1ll << 21;
-__device__ __forceinline__ bool mbar_wait_bounded(unsigned long long* bar, unsigned parity, unsigned* err) {
-    for (long long i = 0; i < kWaitPolls; ++i)
+__device__ __forceinline__ bool mbar_wait_bounded(unsigned long long* bar, unsigned parity, unsigned* err,
+                                                  long long polls = kWaitPolls) {
+    for (long long i = 0; i < polls; ++i)
         if (mbar_try_wait(bar, parity)) return true;
     atomicOr(err, kErrWaitTimeout);
     return false;
