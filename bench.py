@@ -385,8 +385,8 @@ class Timer:
     256 MiB) before every timed op unless the workload is L2-resident by
     design (configuration 1)."""
 
-    def __init__(self, torch, vstream, flush_l2=True):
-        self.torch, self.vstream = torch, vstream
+    def __init__(self, torch, vstream, flush_l2=True, lead_cycles=400_000):
+        self.torch, self.vstream, self.lead_cycles = torch, vstream, lead_cycles
         self.flush_buf = torch.ones(64 << 20, dtype=torch.float32, device="cuda") if flush_l2 else None
         self.flush_out = torch.empty((), dtype=torch.float32, device="cuda")
 
@@ -408,7 +408,7 @@ class Timer:
             # keep the GPU busy while the host queues the step, so the first
             # op's events do not include host launch latency
             with torch.cuda.stream(self.vstream):
-                torch.cuda._sleep(400_000)
+                torch.cuda._sleep(self.lead_cycles)
             for i, (_, _, fn) in enumerate(ops):
                 self.flush()
                 ev[i][0].record(self.vstream)
@@ -601,7 +601,59 @@ def measure_config(name, ctx, torch, vstream, args, barrier):
                       for i, (op, nb, _) in enumerate(ops)}}
     if name == "cfg1":
         res["us_per_step"] = round(step_ms * 1e3, 2)
+        res["roofline_l2"] = l2_roofline(torch, vstream, nbytes, step_ms, per_op_ms, steps, ops)
     return res
+
+
+def l2_roofline(torch, vstream, nbytes, step_ms, per_op_ms, steps, ops):
+    """Configuration 1's 16.8 MB stays in the 126 MB L2, so its ceiling is L2
+    bandwidth, not HBM: measured here as one CUDA graph of 100 back-to-back
+    copies between two 32 MiB buffers that stay L2-resident (read + write
+    bytes / replay time), together with the floor of one empty kernel between
+    the same pair of events (the step is two kernels, replayed as one graph)."""
+    src = torch.ones(8 << 20, dtype=torch.float32, device="cuda")
+    dst = torch.empty_like(src)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            dst.copy_(src)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    reps = 100
+    with torch.cuda.graph(graph, stream=side):
+        for _ in range(reps):
+            dst.copy_(src)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(vstream):
+        graph.replay()
+        times = []
+        for _ in range(5):
+            e0.record(vstream)
+            graph.replay()
+            e1.record(vstream)
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1))
+    l2_gbs = reps * 2 * src.numel() * 4 / (min(times) * 1e-3) / 1e9
+    del graph
+    tiny = torch.zeros(1, dtype=torch.float32, device="cuda")
+    lat = []
+    with torch.cuda.stream(vstream):
+        for _ in range(50):
+            e0.record(vstream)
+            tiny.add_(1.0)
+            e1.record(vstream)
+            torch.cuda.synchronize()
+            lat.append(e0.elapsed_time(e1))
+    floor_us = statistics.median(lat) * 1e3
+    achieved = nbytes / (step_ms * 1e-3) / 1e9
+    return {"bound": "l2", "achieved": round(achieved, 1), "peak": round(l2_gbs, 1), "unit": "GB/s",
+            "peak_kind": "measured L2-resident copy (one graph of 100 copies between two 32 MiB buffers)",
+            "frac": round(achieved / l2_gbs, 3), "bytes_per_step": nbytes,
+            "l2_time_floor_us": round(nbytes / (l2_gbs * 1e9) * 1e6, 2),
+            "empty_kernel_us": round(floor_us, 2), "us_per_step": round(step_ms * 1e3, 2),
+            "note": "the step (one graph of two kernels) against the L2 copy rate; an empty kernel between the "
+                    "same events shows the per-launch floor that dominates a step this small"}
 
 
 def sharded_reduction(args, ctx, timer, barrier, dist, world, rank):
@@ -629,9 +681,7 @@ def sharded_reduction(args, ctx, timer, barrier, dist, world, rank):
     res = {}
 
     def full_op():
-        res["sum0"] = vdist.sum_axis0(xl, sh.count, cols, comm)
-        res["max0"] = vdist.max_axis0(xl, sh.count, cols, comm, sh)
-        res["sum"] = vdist.sum_all(xl, sh.count * cols, comm)
+        res["sum0"], res["max0"], res["sum"] = vdist.axis0_reductions(xl, sh.count, cols, comm, sh)
 
     def p(st):
         return None if st is None else ctypes.c_void_p(st.ptr)
@@ -648,13 +698,21 @@ def sharded_reduction(args, ctx, timer, barrier, dist, world, rank):
                  ctypes.c_size_t(sh.count * cols), ctypes.c_size_t(1), ctypes.c_int64(0), 0, p(pt), None, None)
 
     steps = max(1, args.steps)
-    ms_full = timer.run([("sharded", 0, full_op)], steps, max(3, args.warmup), barrier)[0] / steps
-    ms_local = timer.run([("local", 0, local_op)], steps, 3, barrier)[0] / steps
-    comm.synchronize()
-    t = torch.tensor([ms_full, ms_local], dtype=torch.float64)
+    # a 2 ms lead (GPU sleep) before each step hides the host's enqueue of
+    # the step (partials, the NCCL group, combines) from the device timing
+    dev_timer = Timer(torch, timer.vstream, flush_l2=True, lead_cycles=4_000_000)
+    ms_full = dev_timer.run([("sharded", 0, full_op)], steps, max(3, args.warmup), barrier)[0] / steps
+    ms_local = dev_timer.run([("local", 0, local_op)], steps, 3, barrier)[0] / steps
+    barrier()
+    t0 = time.perf_counter()  # host wall time of back-to-back synchronous steps, for context
+    for _ in range(steps):
+        full_op()
+        comm.synchronize()
+    ms_wall = (time.perf_counter() - t0) * 1e3 / steps
+    t = torch.tensor([ms_full, ms_local, ms_wall], dtype=torch.float64)
     if dist is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_full, ms_local = float(t[0]), float(t[1])
+    ms_full, ms_local, ms_wall = float(t[0]), float(t[1]), float(t[2])
     got = {"sum0": be.download(res["sum0"]), "max0": be.download(res["max0"][0]),
            "arg0": be.download(res["max0"][1]), "sum": be.download(res["sum"])}
     # the 1-GPU results of the whole tensor, on rank 0
@@ -687,8 +745,10 @@ def sharded_reduction(args, ctx, timer, barrier, dist, world, rank):
             "elements_per_s": round(3 * n_global / (ms_full * 1e-3), 1),
             "local_reduce_ms": round(ms_local, 4),
             "collective_and_combine_ms": round(max(0.0, ms_full - ms_local), 4),
+            "host_wall_ms_per_step": round(ms_wall, 4),
             "limiter": ("collective + combine" if ms_full - ms_local > ms_local else "local reduction"),
-            "collective": f"NCCL all-gather over {world} rank(s) (vc_cuda_comm_allgather)",
+            "collective": f"one grouped NCCL all-gather of the four partials per step over {world} rank(s) "
+                          "(vc_cuda_comm_allgather_group)",
             "matches_1gpu": {f"rank{r}": o for r, o in enumerate(oks)}}
 
 

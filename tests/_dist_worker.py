@@ -60,8 +60,15 @@ def main():
     dw = be.upload(w)
     dx = vdist.sum_axis0_backward(dw, sh.count, cols)
     dxm = vdist.sum_axis0_backward(dw, sh.count, cols, mean_rows=rows)
+    s3, (mx3, mi3), tot3 = vdist.axis0_reductions(xl, sh.count, cols, comm, sh)  # one grouped all-gather
     out.update(s=be.download(s), mean=be.download(mean), mx=be.download(mx), mi=be.download(mi),
                tot=float(be.download(tot)[0]), dx=be.download(dx), dxm=be.download(dxm))
+    # the planted NaNs make some sums NaN: compare NaN-aware, bit for bit otherwise
+    grouped_same = (np.array_equal(be.download(s3), out["s"], equal_nan=True) and
+                    np.array_equal(be.download(mx3), out["mx"], equal_nan=True) and
+                    np.array_equal(be.download(mi3), out["mi"]) and
+                    np.array_equal(be.download(tot3), np.array([out["tot"]], np.float32), equal_nan=True))
+    out["grouped_same"] = bool(grouped_same)
 
     # ---- cross-entropy over a sharded batch -----------------------------------------
     batch, classes = 513, 1000
@@ -112,6 +119,7 @@ def main():
             checks[f"rank{r}_sum_axis0"] = rel(res["s"], full_s)
             checks[f"rank{r}_mean_axis0"] = rel(res["mean"], full_mean)
             checks[f"rank{r}_sum_all"] = rel(np.array([res["tot"]]), np.array([full_tot]))
+            checks[f"rank{r}_grouped_allgather_same"] = res["grouped_same"]
             checks[f"rank{r}_max_same_on_every_rank"] = same(res["mx"], gathered[0]["mx"]) and same(res["mi"], gathered[0]["mi"])
         Pt = oracle.port()
         ref_max = Pt.reduce_axis(oracle.MAX, x, 1, rows, cols)

@@ -34,6 +34,8 @@ struct NcclApi {
     ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*){nullptr};
     ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*){nullptr};
     ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t){nullptr};
+    ncclResult_t (*GroupStart)(){nullptr};
+    ncclResult_t (*GroupEnd)(){nullptr};
     ncclResult_t (*CommAbort)(ncclComm_t){nullptr};
     ncclResult_t (*CommDestroy)(ncclComm_t){nullptr};
     const char* (*GetErrorString)(ncclResult_t){nullptr};
@@ -62,6 +64,8 @@ void load_nccl() {
     bind(g_nccl.CommInitRankConfig, "ncclCommInitRankConfig");
     bind(g_nccl.CommGetAsyncError, "ncclCommGetAsyncError");
     bind(g_nccl.AllGather, "ncclAllGather");
+    bind(g_nccl.GroupStart, "ncclGroupStart");
+    bind(g_nccl.GroupEnd, "ncclGroupEnd");
     bind(g_nccl.CommAbort, "ncclCommAbort");
     bind(g_nccl.CommDestroy, "ncclCommDestroy");
     bind(g_nccl.GetErrorString, "ncclGetErrorString");
@@ -78,10 +82,11 @@ void abort_comm_locked() {
 }
 
 // Wait until the communicator leaves ncclInProgress; abort it on error or at
-// the deadline.
+// the deadline. An enqueue normally completes within microseconds: the first
+// polls only yield the thread, later ones sleep 50 us.
 void wait_comm_ready_locked(const char* what) {
     const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(g_timeout_ms);
-    for (;;) {
+    for (int polls = 0;; ++polls) {
         ncclResult_t state = ncclSuccess;
         const ncclResult_t r = g_nccl.CommGetAsyncError(g_comm, &state);
         if (r != ncclSuccess) state = r;
@@ -95,7 +100,10 @@ void wait_comm_ready_locked(const char* what) {
             fail(VC_ERR_TIMEOUT, std::string(what) + " did not finish within " + std::to_string(g_timeout_ms) +
                                      " ms; the communicator was aborted");
         }
-        std::this_thread::sleep_for(std::chrono::microseconds(100));
+        if (polls < 4096)
+            std::this_thread::yield();
+        else
+            std::this_thread::sleep_for(std::chrono::microseconds(50));
     }
 }
 
@@ -156,6 +164,29 @@ vc_status vc_cuda_comm_allgather(const void* send, void* recv, size_t bytes_per_
         fail(VC_ERR_RUNTIME, "ncclAllGather: " + nccl_error(r));
     }
     wait_comm_ready_locked("enqueueing ncclAllGather");
+    VC_API_END
+}
+
+vc_status vc_cuda_comm_allgather_group(const void* const* sends, void* const* recvs, const size_t* bytes_per_rank,
+                                       int count) {
+    VC_API_BEGIN
+    ensure_init();
+    std::lock_guard<std::mutex> lock(g_comm_mutex);
+    if (!g_comm) fail(VC_ERR_INVALID, "comm_allgather_group: no communicator (vc_cuda_comm_init first)");
+    if (count < 0 || (count > 0 && (!sends || !recvs || !bytes_per_rank)))
+        fail(VC_ERR_INVALID, "comm_allgather_group: bad arguments");
+    for (int i = 0; i < count; ++i)
+        if (bytes_per_rank[i] && (!sends[i] || !recvs[i])) fail(VC_ERR_INVALID, "comm_allgather_group: null buffer");
+    ncclResult_t r = g_nccl.GroupStart();
+    for (int i = 0; i < count && (r == ncclSuccess || r == ncclInProgress); ++i)
+        if (bytes_per_rank[i]) r = g_nccl.AllGather(sends[i], recvs[i], bytes_per_rank[i], ncclInt8, g_comm, stream());
+    const ncclResult_t e = g_nccl.GroupEnd();  // always closes the group
+    if (r == ncclSuccess || r == ncclInProgress) r = e;
+    if (r != ncclSuccess && r != ncclInProgress) {
+        abort_comm_locked();
+        fail(VC_ERR_RUNTIME, "grouped ncclAllGather: " + nccl_error(r));
+    }
+    wait_comm_ready_locked("enqueueing the grouped ncclAllGather");
     VC_API_END
 }
 

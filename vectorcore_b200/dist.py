@@ -104,6 +104,18 @@ class Communicator:
                   ctypes.c_size_t(nbytes))
         return recv
 
+    def allgather_group(self, items) -> list:
+        """Several all-gathers as ONE NCCL group (one launch): items are
+        (send storage, bytes per rank, dtype); returns the receive storages
+        ([world * bytes] each, rank-major)."""
+        recvs = [CudaStorage(self.world * nb // np.dtype(dt).itemsize, dt) for _, nb, dt in items]
+        n = len(items)
+        sends = (ctypes.c_void_p * n)(*[s.ptr for s, _, _ in items])
+        rps = (ctypes.c_void_p * n)(*[r.ptr for r in recvs])
+        sizes = (ctypes.c_size_t * n)(*[nb for _, nb, _ in items])
+        _abi.call("vc_cuda_comm_allgather_group", sends, rps, sizes, n)
+        return recvs
+
     def synchronize(self, timeout_ms: int | None = None) -> None:
         _abi.call("vc_cuda_comm_synchronize", int(timeout_ms or self.timeout_ms))
 
@@ -119,24 +131,46 @@ def _p(s):
     return None if s is None else ctypes.c_void_p(s.ptr)
 
 
+def _combine_sum(world: int, gathered: CudaStorage, count: int, divisor: float = 0.0,
+                 negate: bool = False) -> CudaStorage:
+    out = CudaStorage(count)
+    _abi.call("vc_cuda_combine_partials", _B.REDUCE_SUM, _p(gathered), None, None, world, ctypes.c_size_t(count),
+              ctypes.c_float(divisor), int(negate), _p(out), None)
+    return out
+
+
+def _combine_max(world: int, gv: CudaStorage, gi: CudaStorage, count: int):
+    out, idx = CudaStorage(count), CudaStorage(count, np.int64)
+    _abi.call("vc_cuda_combine_partials", _B.REDUCE_MAX, None, _p(gv), _p(gi), world, ctypes.c_size_t(count),
+              ctypes.c_float(0.0), 0, _p(out), _p(idx))
+    return out, idx
+
+
 def _combine_sums(comm: Communicator, partial: CudaStorage, count: int, divisor: float = 0.0,
                   negate: bool = False) -> CudaStorage:
     """All-gather `count` double partials per rank and add them in rank order."""
-    gathered = comm.allgather(partial, count * 8, np.float64)
-    out = CudaStorage(count)
-    _abi.call("vc_cuda_combine_partials", _B.REDUCE_SUM, _p(gathered), None, None, comm.world,
-              ctypes.c_size_t(count), ctypes.c_float(divisor), int(negate), _p(out), None)
-    return out
+    return _combine_sum(comm.world, comm.allgather(partial, count * 8, np.float64), count, divisor, negate)
+
+
+def _partial_sum(x: CudaStorage, rows_local: int, count: int) -> CudaStorage:
+    partial = CudaStorage(count, np.float64)
+    _abi.call("vc_cuda_reduce_axis_partial", _B.REDUCE_SUM, _p(x), ctypes.c_size_t(1), ctypes.c_size_t(rows_local),
+              ctypes.c_size_t(count), ctypes.c_int64(0), 0, _p(partial), None, None)
+    return partial
+
+
+def _partial_max(x: CudaStorage, rows_local: int, count: int, shard: RowShard):
+    pv, pi = CudaStorage(count), CudaStorage(count, np.int64)
+    _abi.call("vc_cuda_reduce_axis_partial", _B.REDUCE_MAX, _p(x), ctypes.c_size_t(1), ctypes.c_size_t(rows_local),
+              ctypes.c_size_t(count), ctypes.c_int64(shard.start), int(shard.rank > 0), None, _p(pv), _p(pi))
+    return pv, pi
 
 
 def sum_axis0(x: CudaStorage, rows_local: int, count: int, comm: Communicator, mean_rows: int = 0) -> CudaStorage:
     """Sum (or the mean over `mean_rows` global rows) over the sharded leading
     axis of x [rows_local, count]: [count] floats, the same on every rank.
     The backward is local: ``sum_axis0_backward``."""
-    partial = CudaStorage(count, np.float64)
-    _abi.call("vc_cuda_reduce_axis_partial", _B.REDUCE_SUM, _p(x), ctypes.c_size_t(1), ctypes.c_size_t(rows_local),
-              ctypes.c_size_t(count), ctypes.c_int64(0), 0, _p(partial), None, None)
-    return _combine_sums(comm, partial, count, float(mean_rows) if mean_rows else 0.0)
+    return _combine_sums(comm, _partial_sum(x, rows_local, count), count, float(mean_rows) if mean_rows else 0.0)
 
 
 def sum_axis0_backward(g: CudaStorage, rows_local: int, count: int, mean_rows: int = 0) -> CudaStorage:
@@ -154,25 +188,38 @@ def max_axis0(x: CudaStorage, rows_local: int, count: int, comm: Communicator, s
     global argmax (int64), with the reference's scan semantics across
     shards: the first maximal row wins (a lower rank wins ties) and a NaN
     only wins at global row 0. Returns (values [count], indices [count])."""
-    pv, pi = CudaStorage(count), CudaStorage(count, np.int64)
-    _abi.call("vc_cuda_reduce_axis_partial", _B.REDUCE_MAX, _p(x), ctypes.c_size_t(1), ctypes.c_size_t(rows_local),
-              ctypes.c_size_t(count), ctypes.c_int64(shard.start), int(shard.rank > 0), None, _p(pv), _p(pi))
-    gv = comm.allgather(pv, count * 4, np.float32)
-    gi = comm.allgather(pi, count * 8, np.int64)
-    out, idx = CudaStorage(count), CudaStorage(count, np.int64)
-    _abi.call("vc_cuda_combine_partials", _B.REDUCE_MAX, None, _p(gv), _p(gi), comm.world, ctypes.c_size_t(count),
-              ctypes.c_float(0.0), 0, _p(out), _p(idx))
-    return out, idx
+    pv, pi = _partial_max(x, rows_local, count, shard)
+    gv, gi = comm.allgather_group([(pv, count * 4, np.float32), (pi, count * 8, np.int64)])
+    return _combine_max(comm.world, gv, gi, count)
 
 
 def sum_all(x: CudaStorage, n_local: int, comm: Communicator, mean_numel: int = 0) -> CudaStorage:
     """Sum (or the mean over `mean_numel` global elements) of every element
     of the sharded tensor: one float, the same on every rank. The backward is
     the upstream broadcast over this rank's shard (``broadcast_to``)."""
+    return _combine_sums(comm, _partial_total(x, n_local), 1, float(mean_numel) if mean_numel else 0.0)
+
+
+def _partial_total(x: CudaStorage, n_local: int) -> CudaStorage:
     partial = CudaStorage(1, np.float64)
     _abi.call("vc_cuda_reduce_axis_partial", _B.REDUCE_SUM, _p(x), ctypes.c_size_t(1), ctypes.c_size_t(n_local),
               ctypes.c_size_t(1), ctypes.c_int64(0), 0, _p(partial), None, None)
-    return _combine_sums(comm, partial, 1, float(mean_numel) if mean_numel else 0.0)
+    return partial
+
+
+def axis0_reductions(x: CudaStorage, rows_local: int, count: int, comm: Communicator, shard: RowShard):
+    """The axis-0 sum, the axis-0 max with its argmax and the full sum of the
+    row-sharded x [rows_local, count] with ONE grouped all-gather of the
+    four partials (one NCCL launch per call instead of four). Returns
+    (sum [count], (max [count], argmax int64 [count]), total [1]), each the
+    same on every rank and equal to the separate calls' results."""
+    ps = _partial_sum(x, rows_local, count)
+    pv, pi = _partial_max(x, rows_local, count, shard)
+    pt = _partial_total(x, rows_local * count)
+    gs, gv, gi, gt = comm.allgather_group([(ps, count * 8, np.float64), (pv, count * 4, np.float32),
+                                           (pi, count * 8, np.int64), (pt, 8, np.float64)])
+    return _combine_sum(comm.world, gs, count), _combine_max(comm.world, gv, gi, count), \
+        _combine_sum(comm.world, gt, 1)
 
 
 def cross_entropy(logits: CudaStorage, targets: CudaStorage, batch_local: int, classes: int,
@@ -233,5 +280,6 @@ def bias_relu_sum_backward(x, b, upstream, rows_local: int, cols: int, comm: Com
     return dx, _combine_sums(comm, part, cols)
 
 
-__all__ = ["RowShard", "Communicator", "exchange_unique_id", "sum_axis0", "sum_axis0_backward", "max_axis0", "sum_all", "cross_entropy", "cross_entropy_backward", "binary_backward",
+__all__ = ["RowShard", "Communicator", "exchange_unique_id", "sum_axis0", "sum_axis0_backward", "max_axis0",
+           "sum_all", "axis0_reductions", "cross_entropy", "cross_entropy_backward", "binary_backward",
            "bias_relu_sum", "bias_relu_sum_backward"]
