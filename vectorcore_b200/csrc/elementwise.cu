@@ -3,9 +3,10 @@
 //
 // Every kernel here is HBM-bandwidth-bound (<= 1 flop per 4 bytes moved), so
 // the design is about bytes in flight and instruction count per byte:
-//  * flat paths (same shape, scalar operand): 128-bit loads/stores, four
-//    independent float4 per thread per iteration, grid = a multiple of the SM
-//    count with a grid-stride loop;
+//  * flat paths (same shape, scalar operand) and their backward rules:
+//    chunked streams -- one short-lived CTA per 16 KiB of each operand, four
+//    float4 per thread, every load issued before the first store (the
+//    stream_grid layout in vc_internal.cuh);
 //  * every other broadcast layout: dimensions are collapsed on the host and
 //    the innermost run of L elements is a "row" (what the reference's CPU
 //    kernel resolves per row, src/cpu/cpu_backend.cpp:59-105). Long float4
@@ -15,8 +16,9 @@
 //    config 5 has 2^32 outputs.
 // Arithmetic is the reference's (src/cpu/cpu_backend.cpp:24-27, 291-316),
 // compiled with -fmad=false and IEEE division so add/sub/mul/div/neg/relu
-// are bit-identical to the CPU path; exp/log/sigmoid use CUDA's
-// full-precision expf/logf.
+// are bit-identical to the CPU path; exp and sigmoid's exponential use
+// exp_acc (a table-driven float exponential, ~0.52 ulp, below) and log uses
+// CUDA's logf, all within 2 ulp of glibc's expf / logf.
 #include "vc_internal.cuh"
 
 #include <algorithm>
@@ -105,6 +107,21 @@ __device__ __forceinline__ float exp_acc(float x) {
     return __int_as_float(__float_as_int(y) + ((n >> 5) << 23));
 }
 
+// num / d for 1 <= d <= 2 and 0 <= num <= 1 (no overflow; only num may be
+// subnormal): Markstein's division -- an approximate reciprocal refined by one
+// Newton-Raphson step, the quotient corrected once with its exact FMA
+// remainder (P. W. Markstein, "Computation of elementary functions on the IBM
+// RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990). A few FMAs where
+// the general IEEE division also handles the ranges this operand pair never
+// reaches; the sweeps check the sigmoid stays within 2 ulp of the reference's.
+__device__ __forceinline__ float div_unit_interval(float num, float d) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(d));
+    y = fmaf(fmaf(-d, y, 1.0f), y, y);
+    const float q = num * y;
+    return fmaf(fmaf(-d, q, num), y, q);
+}
+
 template <int OP>
 __device__ __forceinline__ float uop(float x) {
     if constexpr (OP == VC_NEG) return -x;
@@ -113,12 +130,12 @@ __device__ __forceinline__ float uop(float x) {
     else if constexpr (OP == VC_SIGMOID) {
         // cpu_backend.cpp:302-307 computes 1/(1+exp(-x)) for x >= 0 and
         // e/(1+e) with e = exp(x) otherwise. Both branches evaluate
-        // exp(-|x|), so selecting the numerator gives the same bits with one
+        // exp(-|x|), so selecting the numerator gives the same value with one
         // exponential and one division and no warp divergence (NaN takes the
-        // second form, as in the reference).
+        // second form, as in the reference). 1 + e lies in [1, 2].
         const float e = exp_acc(-fabsf(x));
         const float num = x >= 0.0f ? 1.0f : e;
-        return num / (1.0f + e);
+        return div_unit_interval(num, 1.0f + e);
     } else if constexpr (OP == VC_EXP) return exp_acc(x);
     else return logf(x);
 }
