@@ -796,9 +796,9 @@ def measure_e2e(args, sets, barrier, dist, torch, bytes_global, world, n):
 
     loop(1)  # warm-up: copy streams, events, staging of the first tickets
     # the pipeline fills with one step's upload and drains with one step's
-    # compute and download: time --steps steps (at most 20) so the steady
-    # state dominates, as in a long-running loader
-    steps = max(1, min(args.steps, 20))
+    # compute and download: time 40 steps (~2.6 s) so the steady state
+    # dominates, as in a long-running loader
+    steps = 40
     barrier()
     t0 = time.perf_counter()
     loop(steps)

@@ -867,6 +867,10 @@ row_pipe_kernel(const RowArgs a) {
 __device__ __forceinline__ float fmax4(float4 v) { return fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)); }
 __device__ __forceinline__ bool has_nan4(float4 v) { return v.x != v.x || v.y != v.y || v.z != v.z || v.w != v.w; }
 
+// float4 loads per lane in flight: eight (four CTAs of 8 warps per SM at 56
+// registers) keep more of the row in flight than four (six CTAs at 40).
+constexpr int kCeDepth = 8;
+
 __global__ void __launch_bounds__(kThreads)
 ce_rows_kernel(const RowArgs a) {
     const unsigned lane = threadIdx.x & 31;
@@ -894,11 +898,11 @@ ce_rows_kernel(const RowArgs a) {
             }
         };
         unsigned long long j = lane;
-        for (; j + 96 < L4; j += 128) {
-            float4 v[4];
+        for (; j + 32 * (kCeDepth - 1) < L4; j += 32 * kCeDepth) {
+            float4 v[kCeDepth];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) v[k] = __ldcs(xr + j + 32 * k);
-            take(v, 4);
+            for (int k = 0; k < kCeDepth; ++k) v[k] = __ldcs(xr + j + 32 * k);
+            take(v, kCeDepth);
         }
         for (; j < L4; j += 32) {
             const float4 v = __ldcs(xr + j);
