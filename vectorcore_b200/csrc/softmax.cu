@@ -1032,6 +1032,11 @@ row_reread_kernel(const RowArgs a, unsigned wlog2) {
     const unsigned grp = warp >> wlog2;
     const unsigned gt = ((warp & (W - 1)) << 5) | lane, GT = W << 5;
     const unsigned L4 = static_cast<unsigned>(a.L / 4);  // at most kRereadMaxL / 4
+    // softmax backward: g * y of the first H float4 of each row of the
+    // group, kept in shared memory from pass 1 to pass 2 (dynamic, G * H)
+    extern __shared__ float4 rr_dyn[];
+    const unsigned H = MODE == SM_BWD ? L4 / 2 : 0;
+    float4* sgy = rr_dyn + static_cast<std::size_t>(grp) * H;
     const unsigned long long keep = policy_evict_last(), drop = policy_evict_first();
     const double qnan = static_cast<double>(__int_as_float(0x7fc00000));
 
@@ -1104,7 +1109,9 @@ row_reread_kernel(const RowArgs a, unsigned wlog2) {
 #pragma unroll
                     for (unsigned k = 0; k < D; ++k) {
                         const unsigned jk = min(j + k * GT, L4 - 1);
-                        g[k] = ld4_hint(gr + jk, keep);
+                        // softmax: the first half's g is not read again (its
+                        // g * y waits in shared memory), so L2 need not keep it
+                        g[k] = ld4_hint(gr + jk, MODE == SM_BWD && jk < H ? drop : keep);
                         if constexpr (MODE == SM_BWD) x[k] = ld4_hint(xr + jk, keep);
                     }
 #pragma unroll
@@ -1114,8 +1121,10 @@ row_reread_kernel(const RowArgs a, unsigned wlog2) {
                                 part += quad_sum(neg4(g[k]));
                             } else {
                                 const float4 gv = g[k], xv = x[k];
-                                part += quad_sum(make_float4(-(gv.x * exp_sfu((xv.x - m) - l)), -(gv.y * exp_sfu((xv.y - m) - l)),
-                                                             -(gv.z * exp_sfu((xv.z - m) - l)), -(gv.w * exp_sfu((xv.w - m) - l))));
+                                const float4 gy = make_float4(gv.x * exp_sfu((xv.x - m) - l), gv.y * exp_sfu((xv.y - m) - l),
+                                                              gv.z * exp_sfu((xv.z - m) - l), gv.w * exp_sfu((xv.w - m) - l));
+                                part += quad_sum(neg4(gy));
+                                if (j + k * GT < H) sgy[j + k * GT] = gy;
                             }
                         }
                 }
@@ -1167,27 +1176,34 @@ row_reread_kernel(const RowArgs a, unsigned wlog2) {
             const float de = (dl / s) + 0.0f;
             // LSM_BWD: dx = g + de * expf(x - m)
             // SM_BWD:  dx = gy + de * expf(x - m), gy = g * expf((x - m) - l)
-            auto f = [&](float g, float x) {
-                // softmax: three exponentials per element on the SFU; log_softmax
-                // (one, and at the HBM roofline) keeps expf
-                const float gy = MODE == SM_BWD ? g * exp_sfu((x - m) - l) : g;
+            // softmax: three exponentials per element on the SFU; log_softmax
+            // (one, and at the HBM roofline) keeps expf
+            auto f_gy = [&](float gy, float x) {
                 return gy + de * (MODE == SM_BWD ? exp_sfu(x - m) : expf(x - m));
             };
+            auto f = [&](float g, float x) { return f_gy(MODE == SM_BWD ? g * exp_sfu((x - m) - l) : g, x); };
             // ---------------- pass 2 ----------------
             for (unsigned j = gt; j < L4; j += D * GT) {
                 float4 g[D], x[D];
+                bool have_gy[D];
 #pragma unroll
                 for (unsigned k = 0; k < D; ++k) {
                     const unsigned jk = min(j + k * GT, L4 - 1);
-                    g[k] = ld4_hint(gr + jk, drop);
+                    // softmax, first half: g * y as pass 1 computed it (this
+                    // thread's own shared-memory slots), the same bits
+                    have_gy[k] = MODE == SM_BWD && jk < H;
+                    g[k] = have_gy[k] ? sgy[jk] : ld4_hint(gr + jk, drop);
                     x[k] = MODE == SM_BWD ? ld4_hint(xr + jk, drop) : ld4_stream(reinterpret_cast<const float*>(xr + jk));
                 }
 #pragma unroll
                 for (unsigned k = 0; k < D; ++k)
-                    if (j + k * GT < L4)
-                        st4_stream(reinterpret_cast<float*>(yr + j + k * GT),
-                                   make_float4(f(g[k].x, x[k].x), f(g[k].y, x[k].y), f(g[k].z, x[k].z),
-                                               f(g[k].w, x[k].w)));
+                    if (j + k * GT < L4) {
+                        const float4 o = have_gy[k] ? make_float4(f_gy(g[k].x, x[k].x), f_gy(g[k].y, x[k].y),
+                                                                  f_gy(g[k].z, x[k].z), f_gy(g[k].w, x[k].w))
+                                                    : make_float4(f(g[k].x, x[k].x), f(g[k].y, x[k].y),
+                                                                  f(g[k].z, x[k].z), f(g[k].w, x[k].w));
+                        st4_stream(reinterpret_cast<float*>(yr + j + k * GT), o);
+                    }
             }
         }
     }
@@ -1204,7 +1220,16 @@ static void launch_rows_reread(const RowArgs& a) {
     // per SM walking the rows)
     const unsigned long long ctas = std::min<unsigned long long>((a.rows + rows_per_cta - 1) / rows_per_cta,
                                                                  0x7fffffffull);
-    row_reread_kernel<MODE><<<static_cast<unsigned>(ctas), kRThreads, 0, stream()>>>(a, wlog2);
+    // softmax backward keeps g * y of each row's first half in shared memory
+    // (at most 64 KB per CTA: two CTAs per SM still fit)
+    const std::size_t smem = MODE == SM_BWD ? rows_per_cta * (L4 / 2) * sizeof(float4) : 0;
+    static bool configured = false;
+    if (MODE == SM_BWD && !configured) {
+        VC_CUDA(cudaFuncSetAttribute(row_reread_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(kRereadMaxL / 8 * sizeof(float4))));
+        configured = true;
+    }
+    row_reread_kernel<MODE><<<static_cast<unsigned>(ctas), kRThreads, smem, stream()>>>(a, wlog2);
     check_launch("softmax_rows_reread");
 }
 
