@@ -1033,7 +1033,8 @@ row_reread_kernel(const RowArgs a, unsigned wlog2) {
     const unsigned gt = ((warp & (W - 1)) << 5) | lane, GT = W << 5;
     const unsigned L4 = static_cast<unsigned>(a.L / 4);  // at most kRereadMaxL / 4
     // softmax backward: g * y of the first H float4 of each row of the
-    // group, kept in shared memory from pass 1 to pass 2 (dynamic, G * H)
+    // group, kept in shared memory from pass 1 to pass 2 (dynamic, G * H).
+    // (The same for the forward's x measured slower: 0.93 -> 0.86.)
     extern __shared__ float4 rr_dyn[];
     const unsigned H = MODE == SM_BWD ? L4 / 2 : 0;
     float4* sgy = rr_dyn + static_cast<std::size_t>(grp) * H;
@@ -1222,9 +1223,10 @@ static void launch_rows_reread(const RowArgs& a) {
                                                                  0x7fffffffull);
     // softmax backward keeps g * y of each row's first half in shared memory
     // (at most 64 KB per CTA: two CTAs per SM still fit)
-    const std::size_t smem = MODE == SM_BWD ? rows_per_cta * (L4 / 2) * sizeof(float4) : 0;
+    constexpr bool HALF = MODE == SM_BWD;
+    const std::size_t smem = HALF ? rows_per_cta * (L4 / 2) * sizeof(float4) : 0;
     static bool configured = false;
-    if (MODE == SM_BWD && !configured) {
+    if (HALF && !configured) {
         VC_CUDA(cudaFuncSetAttribute(row_reread_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(kRereadMaxL / 8 * sizeof(float4))));
         configured = true;
