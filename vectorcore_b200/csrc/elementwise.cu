@@ -358,7 +358,7 @@ binary_rows_kernel(const float* __restrict__ a, const float* __restrict__ b, flo
 // cfg5's 17 GB output). Same element values as every other path.
 // ---------------------------------------------------------------------------
 constexpr unsigned kReuseKeep = 4;  // float4 per lane per chunk (512 floats)
-constexpr unsigned kReuseRun = 16;  // k* positions per task
+constexpr unsigned kReuseRun = 16;  // shortest run of k* positions per task
 
 struct ReuseDesc {
     int outer_rank;                      // leading dims other than k*, outer first
@@ -366,6 +366,7 @@ struct ReuseDesc {
     long long x_outer[kMaxRank], y_outer[kMaxRank], o_outer[kMaxRank];
     long long y_step, o_step;            // strides of k* in Y and in the output
     unsigned nq;                         // extent of k*
+    unsigned run;                        // k* positions per task
     unsigned runs, chunks;
     unsigned outer_rows;                 // product of the outer dims (< 2^31)
     unsigned long long tasks;
@@ -406,7 +407,7 @@ binary_reuse_kernel(const float* __restrict__ xp, const float* __restrict__ yp, 
             xv[u] = d.x_inner == 0 ? make_float4(xs, xs, xs, xs)
                                    : (j < d.L4 ? ldg4(xp + xo + 4ll * j) : make_float4(0.f, 0.f, 0.f, 0.f));
         }
-        const unsigned q0 = run * kReuseRun, q1 = min(d.nq, q0 + kReuseRun);
+        const unsigned q0 = run * d.run, q1 = min(d.nq, q0 + d.run);
         unsigned q = q0;
         for (; q + 1 < q1; q += 2) {
             float4 yv[2][kReuseKeep];
@@ -679,8 +680,18 @@ static bool try_launch_reuse(const float* a, const float* b, float* out, const B
     rd.o_step = static_cast<long long>(o_stride[best]);
     rd.L4 = static_cast<unsigned>(d.L / 4);
     rd.chunks = (rd.L4 + 32 * kReuseKeep - 1) / (32 * kReuseKeep);
-    rd.runs = (rd.nq + kReuseRun - 1) / kReuseRun;
-    rd.tasks = static_cast<unsigned long long>(rd.outer_rows) * rd.chunks * rd.runs;
+    // The longest run that still leaves four waves of warps: X's row chunk is
+    // then read once for the whole run instead of once per 16 positions (the
+    // other runs of a row come round long after it left L2: configuration 5
+    // read a eight times from HBM with runs of 16). Every output element is
+    // computed alone, so the split does not change a single value.
+    const unsigned long long want = 4ull * static_cast<unsigned long long>(sm_count()) * (2048 / 32);
+    const unsigned long long per_run = static_cast<unsigned long long>(rd.outer_rows) * rd.chunks;
+    rd.run = rd.nq;
+    while (rd.run > kReuseRun && per_run * ((rd.nq + rd.run - 1) / rd.run) < want) rd.run = (rd.run + 1) / 2;
+    if (rd.run < kReuseRun) rd.run = std::min<unsigned>(kReuseRun, rd.nq);
+    rd.runs = (rd.nq + rd.run - 1) / rd.run;
+    rd.tasks = per_run * rd.runs;
     rd.x_inner = best_x_is_a ? d.a_inner : d.b_inner;
     rd.y_inner = best_x_is_a ? d.b_inner : d.a_inner;
     const std::size_t warps_per_cta = kThreads / 32;
