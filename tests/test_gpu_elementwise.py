@@ -193,11 +193,16 @@ def test_binary_backward(backend, port, a_shape, b_shape):
 # cover V (the dims only b spans) = 128, a non-power-of-two V, a partial
 # 32-float chunk of the inner run, two a-only and two b-only dims
 # interleaved, an outer dim both operands span, and enough a-only positions
-# for many U segments.
+# for many U segments. The TMA-fed kernel takes one V dim of 16, 32, 64 or
+# 128 rows with the inner run a multiple of 64 (V = 128, 64, 32 and 16 below,
+# with one a-only dim or two, one U segment or up to 256); the register
+# kernel the rest (V = 128 with a 96-float run keeps its full-tile path).
 FUSED_CASES = [((8, 1, 64, 256), (1, 128, 1, 256)), ((16, 1, 40, 64), (1, 3, 1, 64)),
                ((4, 1, 50, 96), (1, 100, 1, 96)), ((7, 1, 33, 36), (1, 9, 1, 36)),
                ((1, 6, 1, 10, 16), (4, 1, 5, 1, 16)), ((5, 3, 1, 128), (5, 1, 2, 128)),
-               ((64, 1, 512, 64), (1, 16, 1, 64))]
+               ((64, 1, 512, 64), (1, 16, 1, 64)), ((4, 1, 20, 96), (1, 128, 1, 96)),
+               ((3, 1, 70, 128), (1, 64, 1, 128)), ((300, 1, 192), (1, 32, 192)),
+               ((2, 1, 5, 64), (1, 32, 1, 64))]
 
 
 @pytest.mark.parametrize("a_shape,b_shape", FUSED_CASES)
@@ -217,14 +222,16 @@ def test_binary_backward_two_sided_broadcast(backend, port, a_shape, b_shape):
     backend.synchronize()  # no bounded wait gave up
 
 
-def test_binary_backward_partial_two_sided(backend, port):
+@pytest.mark.parametrize("a_shape,b_shape", [((16, 1, 40, 64), (1, 24, 1, 64)), ((16, 1, 40, 64), (1, 32, 1, 64)),
+                                             ((2, 1, 5, 64), (1, 32, 1, 64))])
+def test_binary_backward_partial_two_sided(backend, port, a_shape, b_shape):
     """The shard-partial entry point returns the unrounded double sums of the
-    same fused pass."""
+    same fused pass (register kernel; TMA-fed kernel with several U segments
+    and with one)."""
     import ctypes
 
     from vectorcore_b200 import _abi
 
-    a_shape, b_shape = (16, 1, 40, 64), (1, 24, 1, 64)
     rng = np.random.default_rng(3)
     a = rng.uniform(0.5, 2, size=a_shape).astype(np.float32)
     b = rng.uniform(0.5, 2, size=b_shape).astype(np.float32)
@@ -240,8 +247,9 @@ def test_binary_backward_partial_two_sided(backend, port):
     got_a = backend.download(pa).view(np.float64).reshape(a_shape)
     got_b = backend.download(pb).view(np.float64).reshape(b_shape)
     ra, rb = port.binary_backward(B.MUL, a, b, g)
-    assert_sum_close(got_a.astype(np.float32), ra, 24, 1.0, what="da partial")
-    assert_sum_close(got_b.astype(np.float32), rb, 640, 1.0, what="db partial")
+    n_b = int(np.prod(out_shape)) // b.size
+    assert_sum_close(got_a.astype(np.float32), ra, b_shape[1], 1.0, what="da partial")
+    assert_sum_close(got_b.astype(np.float32), rb, n_b, 1.0, what="db partial")
 
 
 def test_binary_backward_scalar_upstream(backend, port):

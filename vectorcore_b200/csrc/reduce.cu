@@ -16,6 +16,8 @@
 // SM count), so results do not depend on the launch configuration.
 #include "vc_internal.cuh"
 
+#include <cuda.h>
+
 #include <algorithm>
 #include <cstring>
 #include <mutex>
@@ -1238,6 +1240,364 @@ static void launch_fused_nv(unsigned nv, bool full, const float* g, const float*
     }
 }
 
+// ---------------------------------------------------------------------------
+// The same two-sided broadcast backward, fed by the tensor memory accelerator
+// (TMA), for the shapes where the V rows of g at one u form one tensor-map
+// box: one V dim of 16 * NVT rows (NVT = 1, 2, 4 or 8), no K dims, L a
+// multiple of 64, g dense, a / b strides in whole 16-byte units. g is viewed
+// as the 4-D tensor (l, u1, v, u0) -- innermost first -- whatever the order
+// of its strides.
+//
+// A CTA owns 64 floats of L and a segment of U. One lane of warp 8 (the
+// producer) streams, per u, the [V x 64] tile of g (one 4-D tensor copy) and
+// a's 64 floats (one bulk copy) into a ring of shared-memory stages, each
+// with a "full" mbarrier (completed by the copies' byte count) and an
+// "empty" one (one arrival per consumer warp). The copies of the next stages
+// stay in flight while the 8 consumer warps reduce the current stage, so the
+// kernel does not wait on memory latency at its per-step barrier.
+//
+// Consumer thread (float4 column c = lane & 15, v-group q = 2 * warp +
+// lane / 16) owns the rows v = 16 j + q, j < NVT (its b values stay in
+// registers), per step:
+//   * da[u, 4c .. 4c+3]: its NVT terms folded in float (j order), the two
+//     half-warps added (one shuffle; a + b == b + a), and the 8 warp
+//     partials added in double in warp order by the CTA's first 64 threads,
+//     after a barrier of the consumer warps; da is rounded once;
+//   * db[v, 4c ..]: float blocks of 8 steps flushed into double registers;
+//     at the end each thread writes its own NVT x 4 outputs (or this U
+//     segment's partial, summed in segment order by reduce_col_finish).
+// The combine orders depend on the shape only.
+//
+// Every wait is bounded. A consumer whose wait gives up (error word set)
+// skips the stage; the consumer barrier is a reduction (bar.red.or), so all
+// consumers see the give-up at the same step and leave together, writing
+// nothing. The producer stops issuing when its own wait gives up, and before
+// it returns waits (bounded) for every copy it issued, so no copy lands in a
+// finished CTA's shared memory.
+// ---------------------------------------------------------------------------
+constexpr unsigned kTCols = 64;                  // floats of L per CTA
+constexpr unsigned kTConsumerWarps = 8;
+constexpr unsigned kTConsumers = kTConsumerWarps * 32;
+constexpr unsigned kTThreads = kTConsumers + 32;  // + the producer warp
+constexpr std::size_t kTSmemMax = 227 * 1024;   // opt-in shared memory per CTA
+constexpr unsigned kTMaxStages = 16;
+constexpr unsigned kTFlush = 8;                  // steps per float block of db
+// CTAs to aim for: 4 waves of 148 SMs x 1 resident CTA (a constant: the split,
+// and so the result, depends on the shape alone).
+constexpr unsigned long long kTTargetCtas = 148ull * 4;
+
+struct TmaDesc {
+    unsigned U, U1;
+    FastDiv u1fd;
+    long long ua0, ua1;           // a (= da) strides of the U dims
+    long long vb;                 // b (= db) stride of the V dim
+    unsigned useg, S, stages;
+    unsigned long long db_count;  // elements of db (the partial stride)
+    double* da_d;                 // unrounded outputs (shard partials) when set
+    double* db_d;
+};
+
+// Shared memory of one CTA: alignment slack, [stages][16 NVT][64] g tiles,
+// [stages][64] a rows, [2][8][64] float da partials, [4 NVT][256] double db
+// accumulators (thread-minor), 2 x stages mbarriers.
+template <unsigned NVT>
+static std::size_t tma_smem_fixed() {
+    return 128 + 2 * kTConsumerWarps * kTCols * sizeof(float) + 4ull * NVT * kTConsumers * sizeof(double);
+}
+template <unsigned NVT>
+static std::size_t tma_stage_bytes() {
+    return (16ull * NVT * kTCols + kTCols) * sizeof(float) + 2 * 8;
+}
+template <unsigned NVT>
+static unsigned tma_stages() {
+    return static_cast<unsigned>(std::min<std::size_t>(kTMaxStages, (kTSmemMax - tma_smem_fixed<NVT>()) /
+                                                                         tma_stage_bytes<NVT>()));
+}
+template <unsigned NVT>
+static std::size_t tma_smem(unsigned stages) {
+    return tma_smem_fixed<NVT>() + stages * tma_stage_bytes<NVT>();
+}
+
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, unsigned long long* bar, int x,
+                                            int y, int z, int w) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+        "%5}], [%6];" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<unsigned long long>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_addr(bar))
+        : "memory");
+}
+__device__ __forceinline__ void bulk_load_smem(void* dst, const void* src, unsigned bytes, unsigned long long* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+// Barrier 1 of the consumer warps that also ORs a predicate over them.
+__device__ __forceinline__ bool consumers_sync_or(bool x) {
+    unsigned r;
+    asm volatile(
+        "{\n .reg .pred pin, pout;\n setp.ne.u32 pin, %1, 0;\n bar.red.or.pred pout, 1, %2, pin;\n selp.u32 %0, 1, 0, "
+        "pout;\n}\n"
+        : "=r"(r)
+        : "r"(static_cast<unsigned>(x)), "n"(kTConsumers)
+        : "memory");
+    return r != 0;
+}
+
+template <int OP, unsigned NVT>
+__global__ void __launch_bounds__(kTThreads, 1)
+bcast_backward_tma(const __grid_constant__ CUtensorMap gmap, const float* __restrict__ a,
+                   const float* __restrict__ b, const TmaDesc d, float* __restrict__ da, float* __restrict__ db,
+                   double* __restrict__ partial, unsigned* __restrict__ err) {
+    constexpr bool NEED_AB = OP == VC_MUL || OP == VC_DIV;
+    constexpr unsigned kTile = 16 * NVT * kTCols;  // floats of g per stage
+    extern __shared__ unsigned char tsm_raw[];
+    // stage tiles 128-byte aligned (tensor copy destination)
+    unsigned char* tsm = tsm_raw + ((128 - (smem_addr(tsm_raw) & 127)) & 127);
+    float* gst = reinterpret_cast<float*>(tsm);     // [stages][16 NVT][64]
+    float* ast = gst + d.stages * kTile;            // [stages][64]
+    float* part = ast + d.stages * kTCols;          // [2][8 warps][64]
+    double* dsm = reinterpret_cast<double*>(part + 2 * kTConsumerWarps * kTCols);  // [4 NVT][256]
+    unsigned long long* full = reinterpret_cast<unsigned long long*>(dsm + 4 * NVT * kTConsumers);
+    unsigned long long* empty = full + d.stages;
+
+    const unsigned t = threadIdx.x, w = t >> 5, lane = t & 31;
+    const unsigned l0 = blockIdx.x * kTCols;
+    const unsigned seg = blockIdx.y;
+    const unsigned u0 = seg * d.useg;
+    const unsigned nsteps = min(d.U, u0 + d.useg) - u0;
+    if (t == 0) {
+        for (unsigned s = 0; s < d.stages; ++s) {
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, kTConsumerWarps);
+        }
+        mbar_fence_init();
+    }
+    __syncthreads();
+
+    if (w == kTConsumerWarps) {  // producer
+        if (lane == 0) {
+            constexpr unsigned kTx = (kTile + (NEED_AB ? kTCols : 0)) * sizeof(float);
+            unsigned issued = 0;
+            for (unsigned s = 0; s < nsteps; ++s) {
+                const unsigned slot = s % d.stages;
+                if (s >= d.stages && !mbar_wait_bounded(empty + slot, ((s / d.stages) - 1) & 1u, err)) break;
+                unsigned c0, c1;
+                d.u1fd.divmod(u0 + s, c0, c1);
+                mbar_expect_tx(full + slot, kTx);
+                tma_load_4d(gst + slot * kTile, &gmap, full + slot, static_cast<int>(l0), static_cast<int>(c1), 0,
+                            static_cast<int>(c0));
+                if (NEED_AB)
+                    bulk_load_smem(ast + slot * kTCols,
+                                   a + static_cast<long long>(c0) * d.ua0 + static_cast<long long>(c1) * d.ua1 + l0,
+                                   kTCols * sizeof(float), full + slot);
+                ++issued;
+            }
+            // the last `stages` copies issued land before the CTA may finish
+            for (unsigned s = issued > d.stages ? issued - d.stages : 0; s < issued; ++s)
+                mbar_wait_bounded(full + s % d.stages, (s / d.stages) & 1u, err, kWaitPolls / 16);
+        }
+        return;
+    }
+
+    // consumers
+    const unsigned c = lane & 15, q = 2 * w + (lane >> 4);
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 breg[NVT], facc[NVT];
+    double* dacc = dsm + t;  // element k of this thread: dacc[k * 256]
+#pragma unroll
+    for (unsigned j = 0; j < NVT; ++j) {
+        breg[j] = NEED_AB ? ldg4(b + static_cast<long long>(16 * j + q) * d.vb + l0 + 4 * c) : zero;
+        facc[j] = zero;
+#pragma unroll
+        for (unsigned k = 0; k < 4; ++k) dacc[(4 * j + k) * kTConsumers] = 0.0;
+    }
+    auto flush = [&]() {
+#pragma unroll
+        for (unsigned j = 0; j < NVT; ++j) {
+            dacc[(4 * j + 0) * kTConsumers] += static_cast<double>(facc[j].x);
+            dacc[(4 * j + 1) * kTConsumers] += static_cast<double>(facc[j].y);
+            dacc[(4 * j + 2) * kTConsumers] += static_cast<double>(facc[j].z);
+            dacc[(4 * j + 3) * kTConsumers] += static_cast<double>(facc[j].w);
+            facc[j] = zero;
+        }
+    };
+    bool gave_up = false;
+    for (unsigned s = 0; s < nsteps; ++s) {
+        const unsigned slot = s % d.stages;
+        const bool ok = mbar_wait_bounded(full + slot, (s / d.stages) & 1u, err);
+        float4 dap = zero;
+        if (ok) {
+            const float4* tile = reinterpret_cast<const float4*>(gst + slot * kTile);
+            const float4 av = NEED_AB ? reinterpret_cast<const float4*>(ast + slot * kTCols)[c] : zero;
+#pragma unroll
+            for (unsigned j = 0; j < NVT; ++j) {
+                float4 ga, gb;
+                bb_four<OP>(av, breg[j], tile[(16 * j + q) * (kTCols / 4) + c], ga, gb);
+                dap = j == 0 ? ga : add4(dap, ga);
+                facc[j] = add4(facc[j], gb);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty + slot);
+        dap.x += __shfl_xor_sync(0xffffffffu, dap.x, 16);
+        dap.y += __shfl_xor_sync(0xffffffffu, dap.y, 16);
+        dap.z += __shfl_xor_sync(0xffffffffu, dap.z, 16);
+        dap.w += __shfl_xor_sync(0xffffffffu, dap.w, 16);
+        float* pb = part + (s & 1u) * kTConsumerWarps * kTCols;
+        if (lane < 16) reinterpret_cast<float4*>(pb + w * kTCols)[c] = dap;
+        if (consumers_sync_or(!ok)) {
+            gave_up = true;
+            break;
+        }
+        if (t < kTCols) {
+            double sum = 0.0;
+#pragma unroll
+            for (unsigned k = 0; k < kTConsumerWarps; ++k) sum += static_cast<double>(pb[k * kTCols + t]);
+            unsigned c0, c1;
+            d.u1fd.divmod(u0 + s, c0, c1);
+            const long long off = static_cast<long long>(c0) * d.ua0 + static_cast<long long>(c1) * d.ua1 + l0 + t;
+            if (d.da_d) d.da_d[off] = sum;
+            else da[off] = static_cast<float>(sum);
+        }
+        if ((s + 1) % kTFlush == 0) flush();
+    }
+    if (gave_up) return;
+    flush();
+#pragma unroll
+    for (unsigned j = 0; j < NVT; ++j) {
+        const long long off = static_cast<long long>(16 * j + q) * d.vb + l0 + 4 * c;
+        const double r0 = dacc[(4 * j + 0) * kTConsumers], r1 = dacc[(4 * j + 1) * kTConsumers],
+                     r2 = dacc[(4 * j + 2) * kTConsumers], r3 = dacc[(4 * j + 3) * kTConsumers];
+        if (d.S > 1) {
+            double* p = partial + static_cast<unsigned long long>(seg) * d.db_count + off;
+            p[0] = r0;
+            p[1] = r1;
+            p[2] = r2;
+            p[3] = r3;
+        } else if (d.db_d) {
+            d.db_d[off] = r0;
+            d.db_d[off + 1] = r1;
+            d.db_d[off + 2] = r2;
+            d.db_d[off + 3] = r3;
+        } else {
+            st4(db + off, make_float4(static_cast<float>(r0), static_cast<float>(r1), static_cast<float>(r2),
+                                      static_cast<float>(r3)));
+        }
+    }
+}
+
+template <int OP, unsigned NVT>
+static void launch_tma(const CUtensorMap& map, const float* a, const float* b, const TmaDesc& d, dim3 grid, float* da,
+                       float* db, double* partial) {
+    static bool configured = false;
+    const std::size_t smem = tma_smem<NVT>(d.stages);
+    if (!configured) {
+        VC_CUDA(cudaFuncSetAttribute(bcast_backward_tma<OP, NVT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(tma_smem<NVT>(tma_stages<NVT>()))));
+        configured = true;
+    }
+    bcast_backward_tma<OP, NVT><<<grid, kTThreads, smem, stream()>>>(map, a, b, d, da, db, partial,
+                                                                      device_error_word());
+}
+
+template <int OP>
+static void launch_tma_nvt(unsigned nvt, const CUtensorMap& map, const float* a, const float* b, const TmaDesc& d,
+                           dim3 grid, float* da, float* db, double* partial) {
+    switch (nvt) {
+        case 1: launch_tma<OP, 1>(map, a, b, d, grid, da, db, partial); break;
+        case 2: launch_tma<OP, 2>(map, a, b, d, grid, da, db, partial); break;
+        case 4: launch_tma<OP, 4>(map, a, b, d, grid, da, db, partial); break;
+        default: launch_tma<OP, 8>(map, a, b, d, grid, da, db, partial); break;
+    }
+}
+
+// cuTensorMapEncodeTiled from the driver, looked up once through the runtime
+// (the library does not link libcuda).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            cudaGetLastError();
+            return static_cast<EncodeTiledFn>(nullptr);
+        }
+        return reinterpret_cast<EncodeTiledFn>(p);
+    }();
+    return fn;
+}
+
+// Launch bcast_backward_tma for a classified shape (FusedDesc filled by the
+// caller) when it qualifies; false, having launched nothing, otherwise.
+static bool try_tma_bcast_backward(int op, const float* a, const float* b, const float* g, const FusedDesc& fd,
+                                   float* da, float* db, double* da_d, double* db_d, std::size_t b_numel) {
+    if (fd.nk != 0 || fd.nv != 1 || fd.L % kTCols != 0 || fd.L > 0x7fffffffull) return false;
+    const unsigned V = fd.V;
+    if (V != 16 && V != 32 && V != 64 && V != 128) return false;
+    const bool need_ab = op == VC_MUL || op == VC_DIV;
+    if (fd.vb[0] % 4 != 0 || (need_ab && (fd.ua0 % 4 != 0 || fd.ua1 % 4 != 0))) return false;
+    if (fd.gu0 % 4 != 0 || fd.gu1 % 4 != 0 || fd.vg[0] % 4 != 0) return false;
+    if (fd.U0 > 0x7fffffffu || fd.U1 > 0x7fffffffu) return false;
+    EncodeTiledFn encode = encode_tiled();
+    if (!encode) return false;
+    // g as (l, u1, v, u0); a size-1 dim gets a harmless valid stride
+    const auto stride_of = [&](unsigned size, long long st) -> cuuint64_t {
+        return static_cast<cuuint64_t>(size > 1 ? st : static_cast<long long>(fd.L)) * sizeof(float);
+    };
+    const cuuint64_t dims[4] = {fd.L, fd.U1, V, fd.U0};
+    const cuuint64_t strides[3] = {stride_of(fd.U1, fd.gu1), stride_of(V, fd.vg[0]), stride_of(fd.U0, fd.gu0)};
+    for (cuuint64_t s : strides)
+        if (s % 16 != 0 || s >= (1ull << 40)) return false;
+    const cuuint32_t box[4] = {kTCols, 1, V, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUtensorMap map;
+    if (encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(g), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+
+    TmaDesc d{};
+    d.U = fd.U;
+    d.U1 = fd.U1;
+    d.u1fd = fd.u1fd;
+    d.ua0 = fd.ua0;
+    d.ua1 = fd.ua1;
+    d.vb = fd.vb[0];
+    const unsigned long long chunks = fd.L / kTCols;
+    unsigned long long S = (kTTargetCtas + chunks - 1) / chunks;
+    S = std::max<unsigned long long>(1, std::min<unsigned long long>({S, (fd.U + kFMinUSeg - 1) / kFMinUSeg, 65535}));
+    const unsigned long long useg = (fd.U + S - 1) / S;
+    d.useg = static_cast<unsigned>(useg);
+    d.S = static_cast<unsigned>((fd.U + useg - 1) / useg);
+    d.stages = V == 16 ? tma_stages<1>() : V == 32 ? tma_stages<2>() : V == 64 ? tma_stages<4>() : tma_stages<8>();
+    d.db_count = b_numel;
+    d.da_d = da_d;
+    d.db_d = db_d;
+    if (chunks > 0x7fffffffull) return false;
+
+    Scratch partial(d.S > 1 ? static_cast<std::size_t>(d.S) * b_numel * sizeof(double) : 8);
+    const dim3 grid(static_cast<unsigned>(chunks), d.S, 1);
+    const unsigned nvt = V / 16;
+    switch (op) {
+        case VC_ADD: launch_tma_nvt<VC_ADD>(nvt, map, a, b, d, grid, da, db, partial.as<double>()); break;
+        case VC_SUB: launch_tma_nvt<VC_SUB>(nvt, map, a, b, d, grid, da, db, partial.as<double>()); break;
+        case VC_MUL: launch_tma_nvt<VC_MUL>(nvt, map, a, b, d, grid, da, db, partial.as<double>()); break;
+        default: launch_tma_nvt<VC_DIV>(nvt, map, a, b, d, grid, da, db, partial.as<double>()); break;
+    }
+    check_launch("bcast_backward_tma");
+    if (d.S > 1) {
+        reduce_col_finish<<<grid_for(b_numel, kThreads), kThreads, 0, stream()>>>(partial.as<double>(), d.S, b_numel,
+                                                                                   0.0f, db, db_d);
+        check_launch("bcast_backward_finish");
+    }
+    return true;
+}
+
 // Classify the output dims of a two-sided broadcast backward and launch
 // bcast_backward_fused when the shape fits it (see above; also g dense over
 // the output and every pointer 16-byte aligned). Returns false, having
@@ -1320,6 +1680,7 @@ static bool try_fused_bcast_backward(int op, const float* a, const Src& sa, cons
     d.ua0 = uouter.st[1];
     d.gu1 = uinner.st[0];
     d.gu0 = uouter.st[0];
+    if (try_tma_bcast_backward(op, a, b, g, d, da, db, da_d, db_d, b_numel)) return true;
     unsigned vs = 4;
     while (vs < V && vs < kFRowSlots) vs *= 2;
     d.VS = vs;
