@@ -34,7 +34,10 @@ CASES = [((6, 5), -1), ((6, 5), 0), ((3, 7, 9), 1), ((37, 45), 0), ((64, 1000), 
          ((8, 9000), -1), ((4, 20000), -1), ((4, 32000), -1), ((2, 70000), -1), ((2, 196608), -1),
          ((2, 200003), -1), ((3, 33), -1), ((1, 1), -1),
          # thousands of rows: many clusters per SM, every cluster size
-         ((3000, 1000), -1), ((700, 9000), -1), ((1200, 32000), -1), ((300, 70000), -1), ((2500, 33), -1)]
+         ((3000, 1000), -1), ((700, 9000), -1), ((1200, 32000), -1), ((300, 70000), -1), ((2500, 33), -1),
+         # the forward's shared-memory ring (rows of 8192..40960 floats, in
+         # 2048-float chunks): both ends, a ragged last chunk, rows > SMs
+         ((150, 8192), -1), ((160, 40960), -1), ((149, 10004), -1)]
 
 
 @pytest.mark.parametrize("shape,axis", CASES)

@@ -1333,17 +1333,6 @@ __device__ __forceinline__ void bulk_load_smem(void* dst, const void* src, unsig
         "l"(src), "r"(bytes), "r"(smem_addr(bar))
         : "memory");
 }
-// Barrier 1 of the consumer warps that also ORs a predicate over them.
-__device__ __forceinline__ bool consumers_sync_or(bool x) {
-    unsigned r;
-    asm volatile(
-        "{\n .reg .pred pin, pout;\n setp.ne.u32 pin, %1, 0;\n bar.red.or.pred pout, 1, %2, pin;\n selp.u32 %0, 1, 0, "
-        "pout;\n}\n"
-        : "=r"(r)
-        : "r"(static_cast<unsigned>(x)), "n"(kTConsumers)
-        : "memory");
-    return r != 0;
-}
 
 template <int OP, unsigned NVT>
 __global__ void __launch_bounds__(kTThreads, 1)
@@ -1447,7 +1436,7 @@ bcast_backward_tma(const __grid_constant__ CUtensorMap gmap, const float* __rest
         dap.w += __shfl_xor_sync(0xffffffffu, dap.w, 16);
         float* pb = part + (s & 1u) * kTConsumerWarps * kTCols;
         if (lane < 16) reinterpret_cast<float4*>(pb + w * kTCols)[c] = dap;
-        if (consumers_sync_or(!ok)) {
+        if (named_barrier_or<1, kTConsumers>(!ok)) {
             gave_up = true;
             break;
         }

@@ -1235,6 +1235,231 @@ static void launch_rows_reread(const RowArgs& a) {
     check_launch("softmax_rows_reread");
 }
 
+// ---------------------------------------------------------------------------
+// Softmax / log_softmax forward on aligned rows of kRingMinL..kRingMaxL
+// floats, ring design: one CTA per SM walks the rows blockIdx.x,
+// blockIdx.x + gridDim.x, ... One lane of warp 16 (the producer) bulk-copies
+// each row TWICE, in chunks of kRingChunk floats, into a ring of kRingSlots
+// shared-memory slots: first for pass 1 (from HBM, L2 evict_last), then
+// straight away for pass 2 (an L2 hit by then, evict_first). Each slot has a
+// "full" mbarrier (completed by the copy's byte count) and an "empty" one
+// (one arrival per consumer warp); the consumers release a chunk as soon as
+// they have used it, so the producer streams without pause and the
+// consumers issue no loads at all. (The re-read kernel issues its loads
+// from the consumer threads, so HBM idles while its CTAs reduce and write.
+// Measured on the way here: the whole row kept in the ring until pass 2,
+// which left too few slots for the next row, 0.80 of the copy peak; pass 1
+// from the ring and pass 2 as consumer loads from L2, 0.64; 8 KB chunks, one
+// float4 per thread each, 0.59 -- 43 instructions per element, the slot
+// bookkeeping of every wait.)
+// 16 consumer warps; thread t handles float4 t + 512 k (k < 4) of every
+// chunk; both sides walk the ring with running (slot, phase) counters:
+//   pass 1: per chunk, its maximum first (NaN never wins, positions past
+//           the row's end count as -inf), the running sum rescaled at most
+//           once per chunk, the chunk's terms added in float and its total
+//           in double (the re-read kernel's arithmetic);
+//   combine: per-warp (max, sum) through shared memory (double-buffered by
+//           row parity) at a barrier of the consumer warps that also ORs
+//           their wait give-ups, so all leave at the same row;
+//   pass 2: the row's second copy, outputs written once (streaming stores).
+// Every wait is bounded; a give-up skips the rest of the row's waits and
+// stores and reaches every consumer at the next barrier. The producer stops
+// issuing when its wait gives up and, before it returns, waits (bounded) for
+// the copies it issued.
+// ---------------------------------------------------------------------------
+constexpr unsigned kRingChunk = 8192;                     // floats per slot (32 KB)
+constexpr unsigned kRingChunk4 = kRingChunk / 4;
+constexpr unsigned kRingSlots = 6;
+constexpr unsigned kRingConsumerWarps = 16;
+constexpr unsigned kRingConsumers = kRingConsumerWarps * 32;
+constexpr unsigned kRingPer = kRingChunk4 / kRingConsumers;  // float4 of a chunk per thread
+constexpr unsigned kRingThreads = kRingConsumers + 32;
+constexpr unsigned long long kRingMinL = 8192;
+constexpr unsigned long long kRingMaxL = 40960;
+
+constexpr std::size_t ring_smem() {
+    return 128 + static_cast<std::size_t>(kRingSlots) * kRingChunk * sizeof(float) +
+           2 * kRingConsumerWarps * sizeof(double2) + 2 * kRingSlots * sizeof(unsigned long long);
+}
+
+__device__ __forceinline__ void bulk_load_hint(void* dst, const void* src, unsigned bytes, unsigned long long* bar,
+                                               unsigned long long policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kRingThreads, 1)
+row_ring_kernel(const RowArgs a) {
+    extern __shared__ unsigned char ring_raw[];
+    unsigned char* base = ring_raw + ((128 - (smem_addr(ring_raw) & 127)) & 127);
+    float4* ring = reinterpret_cast<float4*>(base);  // [slots][kRingChunk4]
+    double2* wslots = reinterpret_cast<double2*>(ring + kRingSlots * kRingChunk4);  // [2][16]
+    unsigned long long* full = reinterpret_cast<unsigned long long*>(wslots + 2 * kRingConsumerWarps);
+    unsigned long long* empty = full + kRingSlots;
+
+    const unsigned t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const unsigned long long L = a.L;
+    const unsigned L4 = static_cast<unsigned>(L / 4);
+    const unsigned R = static_cast<unsigned>((L + kRingChunk - 1) / kRingChunk);  // chunks per row
+    if (t == 0) {
+        for (unsigned s = 0; s < kRingSlots; ++s) {
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, kRingConsumerWarps);
+        }
+        mbar_fence_init();
+    }
+    __syncthreads();
+
+    if (warp == kRingConsumerWarps) {  // producer
+        if (lane == 0) {
+            const unsigned long long keep = policy_evict_last(), drop = policy_evict_first();
+            unsigned slot = 0, phase = 0, issued = 0;
+            bool stop = false;
+            for (unsigned long long row = blockIdx.x; row < a.rows && !stop; row += gridDim.x) {
+                const float* xr = a.x + row * L;
+                for (unsigned cc = 0; cc < 2 * R; ++cc) {  // pass 1's copy, then pass 2's
+                    const unsigned c = cc < R ? cc : cc - R;
+                    // the slot's previous chunk (one lap earlier) has been released
+                    if (issued >= kRingSlots && !mbar_wait_bounded(empty + slot, phase ^ 1u, a.err)) {
+                        stop = true;
+                        break;
+                    }
+                    const unsigned long long rest = L - static_cast<unsigned long long>(c) * kRingChunk;
+                    const unsigned bytes = static_cast<unsigned>(rest < kRingChunk ? rest : kRingChunk) * 4u;
+                    mbar_expect_tx(full + slot, bytes);
+                    bulk_load_hint(ring + slot * kRingChunk4, xr + static_cast<unsigned long long>(c) * kRingChunk,
+                                   bytes, full + slot, cc < R ? keep : drop);
+                    ++issued;
+                    if (++slot == kRingSlots) {
+                        slot = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            // the last copies issued land before the CTA may finish
+            for (unsigned k = issued > kRingSlots ? issued - kRingSlots : 0; k < issued; ++k)
+                mbar_wait_bounded(full + k % kRingSlots, (k / kRingSlots) & 1u, a.err, kWaitPolls / 16);
+        }
+        return;
+    }
+
+    // consumers
+    const double qnan = static_cast<double>(__int_as_float(0x7fc00000));
+    unsigned slot = 0, phase = 0;
+    auto next_slot = [&]() {
+        if (++slot == kRingSlots) {
+            slot = 0;
+            phase ^= 1u;
+        }
+    };
+    auto release = [&]() {  // this warp is done with the chunk in `slot`
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty + slot);
+        next_slot();
+    };
+    unsigned it = 0;
+    bool ok = true;  // no wait has given up (a pass-2 give-up reaches the next row's barrier)
+    for (unsigned long long row = blockIdx.x; row < a.rows; row += gridDim.x, ++it) {
+        // ---------------- pass 1 ----------------
+        float m = -INFINITY;
+        double s = 0.0;
+        bool nan_seen = false;
+        for (unsigned c = 0; c < R; ++c) {
+            if (ok) ok = mbar_wait_bounded(full + slot, phase, a.err);  // one give-up ends the waits
+            float4 v[kRingPer];
+            const float4* ch = ring + slot * kRingChunk4;
+#pragma unroll
+            for (unsigned k = 0; k < kRingPer; ++k) {
+                const unsigned q = c * kRingChunk4 + k * kRingConsumers + t;
+                v[k] = ok && q < L4 ? ch[k * kRingConsumers + t] : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+            }
+            float bm = -INFINITY;
+#pragma unroll
+            for (unsigned k = 0; k < kRingPer; ++k) bm = fmaxf(bm, fmaxf(fmaxf(v[k].x, v[k].y), fmaxf(v[k].z, v[k].w)));
+            release();  // the chunk's values are in registers
+            if (bm > m) {  // NaN never compares greater
+                if (m != -INFINITY) s *= static_cast<double>(expf(m - bm));
+                m = bm;
+            }
+            if (m == -INFINITY) {  // nothing but -inf (and NaN) so far: no terms yet
+#pragma unroll
+                for (unsigned k = 0; k < kRingPer; ++k)
+                    nan_seen = nan_seen || v[k].x != v[k].x || v[k].y != v[k].y || v[k].z != v[k].z ||
+                               v[k].w != v[k].w;
+            } else {
+                float r = 0.0f;
+#pragma unroll
+                for (unsigned k = 0; k < kRingPer; ++k)
+                    r += (exp_term(v[k].x - m) + exp_term(v[k].y - m)) + (exp_term(v[k].z - m) + exp_term(v[k].w - m));
+                s += static_cast<double>(r);
+            }
+        }
+        const float mw = warp_fmax(m);
+        double tw = m == -INFINITY ? (nan_seen ? qnan : 0.0) : s * static_cast<double>(expf(m - mw));
+        tw = warp_sum(tw);
+        if (__any_sync(0xffffffffu, nan_seen)) tw = qnan;
+        double2* sl = wslots + (it & 1u) * kRingConsumerWarps;
+        if (lane == 0) sl[warp] = make_double2(static_cast<double>(mw), tw);
+        if (named_barrier_or<1, kRingConsumers>(!ok)) return;  // a wait gave up: this row is not written
+
+        // ---------------- combine the 16 warps (the same order in each) ----------------
+        float mm = lane < kRingConsumerWarps ? static_cast<float>(sl[lane].x) : -INFINITY;
+        mm = warp_fmax(mm);
+        const double tq =
+            lane < kRingConsumerWarps ? sl[lane].y * static_cast<double>(expf(static_cast<float>(sl[lane].x) - mm)) : 0.0;
+        double s_row = warp_sum(tq);
+        if (mm == -INFINITY) s_row = qnan;  // a row of -inf only: the reference's x - m is NaN everywhere
+        float mrow = mm;
+        const float* xr = a.x + row * L;
+        const float first = __ldg(xr);
+        if (first != first) mrow = first;  // the scan never leaves a NaN at index 0
+        else if (mrow == 0.0f) mrow = first_zero(xr, L4, lane);
+        const float srow = static_cast<float>(s_row);
+        const float l = logf(srow);
+        if (t == 0) {
+            if (a.row_max) a.row_max[row] = mrow;
+            if (a.row_sum) a.row_sum[row] = srow;
+        }
+        auto f = [&](float v) {
+            const float ls = (v - mrow) - l;
+            return MODE == SM_FWD ? exp_sfu(ls) : ls;
+        };
+        // ---------------- pass 2 ----------------
+        float4* yr = reinterpret_cast<float4*>(a.y + row * L);
+        for (unsigned c = 0; c < R; ++c) {
+            if (ok) ok = mbar_wait_bounded(full + slot, phase, a.err);
+            const float4* ch = ring + slot * kRingChunk4;
+            float4 v[kRingPer];
+#pragma unroll
+            for (unsigned k = 0; k < kRingPer; ++k) v[k] = ch[k * kRingConsumers + t];
+#pragma unroll
+            for (unsigned k = 0; k < kRingPer; ++k) {
+                const unsigned q = c * kRingChunk4 + k * kRingConsumers + t;
+                if (ok && q < L4)
+                    st4_stream(reinterpret_cast<float*>(yr + q), make_float4(f(v[k].x), f(v[k].y), f(v[k].z), f(v[k].w)));
+            }
+            release();
+        }
+    }
+}
+
+template <int MODE>
+static void launch_rows_ring(const RowArgs& a) {
+    static bool configured = false;
+    if (!configured) {
+        VC_CUDA(cudaFuncSetAttribute(row_ring_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(ring_smem())));
+        configured = true;
+    }
+    const unsigned long long ctas = std::min<unsigned long long>(a.rows, static_cast<unsigned long long>(sm_count()));
+    row_ring_kernel<MODE><<<static_cast<unsigned>(ctas), kRingThreads, ring_smem(), stream()>>>(a);
+    check_launch("softmax_rows_ring");
+}
+
 template <int MODE, bool BULK>
 static void launch_rows_mode(const RowArgs& a, unsigned C, std::size_t smem) {
     static bool configured = false;
@@ -1329,6 +1554,12 @@ static void launch_family(RowArgs a, std::size_t outer, std::size_t length, std:
             ce_rows_kernel<<<static_cast<unsigned>(ctas), kThreads, 0, stream()>>>(a);
             check_launch("cross_entropy_rows");
             return;
+        }
+        if constexpr (MODE == LSM_FWD || MODE == SM_FWD) {
+            if (aligned && length >= kRingMinL && length <= kRingMaxL) {
+                launch_rows_ring<MODE>(a);
+                return;
+            }
         }
         if constexpr (MODE != CE_FWD) {
             if (aligned && length <= kRereadMaxL) {

@@ -251,6 +251,23 @@ __device__ __forceinline__ bool mbar_wait_bounded(unsigned long long* bar, unsig
     return false;
 }
 
+// Named barrier ID (1..15) of the CTA's first N threads (a multiple of 32)
+// that also returns the OR of a predicate over them: a producer/consumer
+// kernel's consumers meet here without the producer warp, and a wait that
+// gave up in any consumer reaches all of them at the same barrier.
+template <unsigned ID, unsigned N>
+__device__ __forceinline__ bool named_barrier_or(bool x) {
+    static_assert(ID >= 1 && ID < 16 && N % 32 == 0, "named barrier");
+    unsigned r;
+    asm volatile(
+        "{\n .reg .pred pin, pout;\n setp.ne.u32 pin, %1, 0;\n bar.red.or.pred pout, %2, %3, pin;\n selp.u32 %0, 1, "
+        "0, pout;\n}\n"
+        : "=r"(r)
+        : "r"(static_cast<unsigned>(x)), "n"(ID), "n"(N)
+        : "memory");
+    return r != 0;
+}
+
 // Max/argmax candidate under the reference's scan semantics: a larger value
 // wins; equal values (==, so -0 == +0) keep the smaller index; NaN is never
 // a candidate (the caller applies the "NaN at index 0 wins" rule).
