@@ -82,7 +82,8 @@ def main():
     out.update(loss=float(be.download(loss)[0]), dlogits=be.download(dlg))
 
     # ---- gradient of a replicated broadcast operand (configuration 5's b) ----------
-    P, Q, R, L = 5, 8, 24, 64
+    # (16 rows of b: the TMA-fed kernel, with double db partials per shard)
+    P, Q, R, L = 5, 16, 24, 64
     a5 = np.random.default_rng(7).uniform(-1, 1, (P, 1, R, L)).astype(np.float32)
     b5 = np.random.default_rng(8).uniform(-1, 1, (1, Q, 1, L)).astype(np.float32)
     g5 = np.random.default_rng(9).uniform(-1, 1, (P, Q, R, L)).astype(np.float32)
