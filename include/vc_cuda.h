@@ -249,7 +249,11 @@ vc_status vc_cuda_scatter_axis(const float* values, const float* indices_f32,
 vc_status vc_cuda_reduce_axis_backward(int op, const float* g, const int64_t* indices,
                                        float* out, size_t outer, size_t length, size_t inner);
 
-/* ---- softmax family (fused, one CTA cluster per row) ------------------------ */
+/* ---- softmax family (fused: HBM reads each input once) ---------------------- */
+/* Rows of 8192-40960 floats (forward) stream through a ring of shared-memory
+ * slots fed by bulk copies, one CTA per SM; shorter rows and the backward use
+ * one CTA per row group with an L2 re-read; longer rows a CTA cluster per
+ * row; other axes a column kernel. All give the same results contract. */
 
 /* y = log_softmax / softmax of x along the middle axis of [outer, length,
  * inner], computed as the reference does (src/ops.cpp:378-388): m = row max,
