@@ -585,8 +585,11 @@ def wl_metric(name):
 def measure_config(name, ctx, torch, vstream, args, barrier):
     """Per-op GB/s of another configuration at its full shape on this GPU
     (same timing rules as the headline: warm-up, CUDA events, L2 flush)."""
+    # allocated as the headline path does (torch keeps its generator
+    # temporaries cached while the configuration is timed; release() frees
+    # everything afterwards): emptying torch's cache here moved where the
+    # 8.4 GB configuration-4 outputs landed and measured 4% slower
     wl = WORKLOADS[name](ctx)
-    torch.cuda.empty_cache()
     ops = wl["ops"]
     steps = max(1, min(args.steps, 5))
     per_op_ms = Timer(torch, vstream, flush_l2=name != "cfg1").run(ops, steps, 3, barrier)
