@@ -383,7 +383,8 @@ WORKLOADS = {"cfg1": wl_cfg1, "cfg2": wl_cfg2, "cfg3": wl_cfg3, "cfg4": wl_cfg4,
 class Timer:
     """Per-op CUDA events on the library's stream, with an L2 flush (a read of
     256 MiB) before every timed op unless the workload is L2-resident by
-    design (configuration 1)."""
+    design (configuration 1), and a GPU sleep of `lead_cycles` between the
+    flush and the op's start event."""
 
     def __init__(self, torch, vstream, flush_l2=True, lead_cycles=400_000):
         self.torch, self.vstream, self.lead_cycles = torch, vstream, lead_cycles
@@ -405,12 +406,14 @@ class Timer:
         ev = [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in ops]
         per_op_ms = [0.0] * len(ops)
         for _ in range(steps):
-            # keep the GPU busy while the host queues the step, so the first
-            # op's events do not include host launch latency
-            with torch.cuda.stream(self.vstream):
-                torch.cuda._sleep(self.lead_cycles)
             for i, (_, _, fn) in enumerate(ops):
                 self.flush()
+                # keep the GPU busy while the host queues the op, so its
+                # events hold no host launch latency (outside the events, like
+                # the flush; with one lead per step instead, the first op of
+                # every step read up to 10% slow)
+                with torch.cuda.stream(self.vstream):
+                    torch.cuda._sleep(self.lead_cycles)
                 ev[i][0].record(self.vstream)
                 fn()
                 ev[i][1].record(self.vstream)
