@@ -1269,7 +1269,7 @@ static void launch_rows_reread(const RowArgs& a) {
 // ---------------------------------------------------------------------------
 constexpr unsigned kRingChunk = 8192;                     // floats per slot (32 KB)
 constexpr unsigned kRingChunk4 = kRingChunk / 4;
-constexpr unsigned kRingSlots = 6;
+constexpr unsigned kRingSlots = 7;
 constexpr unsigned kRingConsumerWarps = 16;
 constexpr unsigned kRingConsumers = kRingConsumerWarps * 32;
 constexpr unsigned kRingPer = kRingChunk4 / kRingConsumers;  // float4 of a chunk per thread
