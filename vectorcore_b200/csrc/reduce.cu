@@ -322,6 +322,7 @@ reduce_col_simple(const float* __restrict__ g, const float* __restrict__ p, cons
 __global__ void __launch_bounds__(kThreads)
 reduce_col_finish(const double* __restrict__ partial, unsigned S, unsigned long long count,
                   float divisor, float* __restrict__ out, double* __restrict__ out_d) {
+    pdl_wait();  // a programmatic launch: the partials' kernel has finished and its writes are visible
     const unsigned long long stride = static_cast<unsigned long long>(gridDim.x) * blockDim.x;
     for (unsigned long long o = static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x; o < count;
          o += stride) {
@@ -363,6 +364,7 @@ __global__ void __launch_bounds__(kSliceThreads)
 reduce_col_finish_sliced(const double* __restrict__ partial, unsigned S, unsigned long long count,
                          float divisor, float* __restrict__ out, double* __restrict__ out_d,
                          unsigned long long rep) {
+    pdl_wait();  // a programmatic launch: the partials' kernel has finished and its writes are visible
     __shared__ double s_slice[kSlices][32];
     __shared__ float s_res[32];
     const unsigned lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -575,6 +577,7 @@ reduce_row_kernel(const float* __restrict__ g, const float* __restrict__ p, cons
 __global__ void __launch_bounds__(kFinishWideThreads)
 reduce_row_finish(const double* __restrict__ partial, unsigned S, unsigned long long K, float divisor,
                   float* __restrict__ out, double* __restrict__ out_d) {
+    pdl_wait();  // a programmatic launch: the partials' kernel has finished and its writes are visible
     __shared__ double s_red[32];
     for (unsigned long long k = blockIdx.x; k < K; k += gridDim.x) {
         double acc = 0.0;
@@ -778,12 +781,14 @@ static bool launch_vjp_reduce(const Src ops[3], const size_t* src_shape, int src
             const unsigned long long count = d.K * d.inner;
             // shape-only choice: the order of the additions is part of the result
             if (d.S >= 2 * kSlices && count <= kSlicedMaxOutputs) {
-                reduce_col_finish_sliced<<<static_cast<unsigned>((count + 31) / 32), kSliceThreads, 0, stream()>>>(
-                    partial.as<double>(), d.S, count, divisor, out, out_d, out_d ? 1 : rep);
+                launch_pdl(reduce_col_finish_sliced, dim3(static_cast<unsigned>((count + 31) / 32)), dim3(kSliceThreads), 0,
+                           stream(), partial.as<double>(), d.S, count, divisor, out, out_d,
+                           out_d ? 1ull : static_cast<unsigned long long>(rep));
                 check_launch("reduce_col_finish");
                 return true;
             }
-            reduce_col_finish<<<grid_for(count, kThreads), kThreads, 0, stream()>>>(partial.as<double>(), d.S, count, divisor, out, out_d);
+            launch_pdl(reduce_col_finish, dim3(grid_for(count, kThreads)), dim3(kThreads), 0, stream(), partial.as<double>(),
+                       d.S, count, divisor, out, out_d);
             check_launch("reduce_col_finish");
         }
         return rep == 1;
@@ -829,8 +834,9 @@ static bool launch_vjp_reduce(const Src ops[3], const size_t* src_shape, int src
 #undef VC_ROW
     check_launch("reduce_row");
     if (d.S > 1) {
-        reduce_row_finish<<<static_cast<unsigned>(std::min<unsigned long long>(d.K, static_cast<unsigned long long>(sm_count()) * 8)),
-                            row_finish_threads(d.K, d.S), 0, stream()>>>(partial.as<double>(), d.S, d.K, divisor, out, out_d);
+        launch_pdl(reduce_row_finish,
+                   dim3(static_cast<unsigned>(std::min<unsigned long long>(d.K, static_cast<unsigned long long>(sm_count()) * 8))),
+                   dim3(row_finish_threads(d.K, d.S)), 0, stream(), partial.as<double>(), d.S, d.K, divisor, out, out_d);
         check_launch("reduce_row_finish");
     }
     return rep == 1;
@@ -1773,6 +1779,7 @@ max_row_kernel(const float* __restrict__ in, unsigned long long outer, unsigned 
 __global__ void __launch_bounds__(kFinishWideThreads)
 max_row_finish(const float* __restrict__ in, unsigned long long outer, unsigned long long length, unsigned S,
                const float* __restrict__ pv, const long long* __restrict__ pi, MaxOut o) {
+    pdl_wait();  // a programmatic launch: the partials' kernel has finished and its writes are visible
     // One CTA per row. max_combine (larger value, then smaller index) is
     // associative and commutative, so the tree order cannot change the result.
     __shared__ float s_v[32];
@@ -1848,6 +1855,7 @@ __global__ void __launch_bounds__(kThreads)
 max_col_finish(const float* __restrict__ in, unsigned long long outer, unsigned long long length,
                unsigned long long inner, unsigned S, const float* __restrict__ pv,
                const long long* __restrict__ pi, MaxOut o) {
+    pdl_wait();  // a programmatic launch: the partials' kernel has finished and its writes are visible
     const unsigned long long count = outer * inner;
     const unsigned long long stride = static_cast<unsigned long long>(gridDim.x) * blockDim.x;
     for (unsigned long long k = static_cast<unsigned long long>(blockIdx.x) * blockDim.x + threadIdx.x; k < count;
@@ -1884,8 +1892,10 @@ static void launch_max(const float* in, std::size_t outer, std::size_t length, s
         else max_row_kernel<false><<<grid, kThreads, 0, st>>>(in, outer, length, seg, Sn, o, pv.as<float>(), pi.as<long long>());
         check_launch("max_row");
         if (Sn > 1) {
-            max_row_finish<<<static_cast<unsigned>(std::min<std::size_t>(outer, static_cast<std::size_t>(sm_count()) * 8)),
-                             row_finish_threads(outer, Sn), 0, st>>>(in, outer, length, Sn, pv.as<float>(), pi.as<long long>(), o);
+            launch_pdl(max_row_finish,
+                       dim3(static_cast<unsigned>(std::min<std::size_t>(outer, static_cast<std::size_t>(sm_count()) * 8))),
+                       dim3(row_finish_threads(outer, Sn)), 0, st, in, static_cast<unsigned long long>(outer),
+                       static_cast<unsigned long long>(length), Sn, pv.as<float>(), pi.as<long long>(), o);
             check_launch("max_row_finish");
         }
         return;
@@ -1905,7 +1915,9 @@ static void launch_max(const float* in, std::size_t outer, std::size_t length, s
     else max_col_kernel<false><<<grid, kThreads, 0, st>>>(in, outer, length, inner, seg, Sn, o, pv.as<float>(), pi.as<long long>());
     check_launch("max_col");
     if (Sn > 1) {
-        max_col_finish<<<grid_for(outer * inner, kThreads), kThreads, 0, st>>>(in, outer, length, inner, Sn, pv.as<float>(), pi.as<long long>(), o);
+        launch_pdl(max_col_finish, dim3(grid_for(outer * inner, kThreads)), dim3(kThreads), 0, st, in,
+                   static_cast<unsigned long long>(outer), static_cast<unsigned long long>(length),
+                   static_cast<unsigned long long>(inner), Sn, pv.as<float>(), pi.as<long long>(), o);
         check_launch("max_col_finish");
     }
 }
