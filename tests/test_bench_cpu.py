@@ -42,3 +42,32 @@ def test_reference_arm_prints_one_json_line():
     assert d["higher_is_better"] is True and d["metric"].startswith("effective HBM GB/s (config 2")
     assert d["cpu_baseline"]["kind"] == "reference" and d["cpu_baseline"]["cores"] >= 1
     assert d["e2e"] == {"value": d["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+class _Done:
+    def __init__(self, returncode, stdout, stderr=""):
+        self.returncode, self.stdout, self.stderr = returncode, stdout, stderr
+
+
+def test_per_configuration_child_command_and_its_json_line(monkeypatch):
+    """The default run times each extra configuration in a child process
+    (`bench.py --config-only cfgN`) and takes the child's last JSON line; a
+    child that fails is reported with its configuration's name."""
+    import argparse
+
+    seen = {}
+
+    def fake_run(cmd, **kw):
+        seen["cmd"], seen["env"] = cmd, kw.get("env", {})
+        return _Done(0, 'log line\n{"value": 1.5, "per_op": {}}\n')
+
+    monkeypatch.setenv("RANK", "0")
+    monkeypatch.setattr(bench.subprocess, "run", fake_run)
+    got = bench.config_in_child("cfg4", argparse.Namespace(steps=20))
+    assert got == {"value": 1.5, "per_op": {}}
+    assert seen["cmd"][1:] == [str(ROOT / "bench.py"), "--config-only", "cfg4", "--steps", "20"]
+    assert "RANK" not in seen["env"]  # the child is a one-GPU process of its own
+
+    monkeypatch.setattr(bench.subprocess, "run", lambda cmd, **kw: _Done(3, "", "CUDA error"))
+    with pytest.raises(RuntimeError, match="cfg4.*exit 3"):
+        bench.config_in_child("cfg4", argparse.Namespace(steps=5))
